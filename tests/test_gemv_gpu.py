@@ -1,0 +1,281 @@
+"""GPU parity tests of the decode-GEMV kernels, through the C ABI.
+
+Each case quantises seeded inputs, runs the sm_100a kernel and compares it with
+the CPU oracle (the reference's scalar arithmetic restated in
+oracle/quant_oracle.c), at the bar of BASELINE.json: cos >= 0.999999 and
+max-abs error <= 1e-4 * max|y|.  The test intents follow the reference's own
+suites: tests/test-gemv-accuracy.cpp (accuracy, zero invariance, boundary N,
+model shapes, K validation, concurrency) and tests/test-kquants-gemv.cpp
+(per-type accuracy, zero invariance, shape sweep).
+"""
+import ctypes as C
+import threading
+
+import numpy as np
+import pytest
+
+from helpers import check_parity, gemv_gpu, normal_weights, normal_x, random_blocks, to_dev
+
+pytestmark = pytest.mark.gpu
+
+TYPES = ["Q4_0", "Q3_K", "Q4_K", "Q5_K", "Q6_K", "IQ3_XXS", "IQ3_S", "IQ2_S", "IQ4_XS"]
+# (N, K): one full-tile case, odd row counts (partial last tile), an odd super-block count
+SHAPES = [(64, 512), (33, 768), (127, 256), (6, 256 * 43), (1, 256)]
+
+
+@pytest.mark.parametrize("name", TYPES)
+@pytest.mark.parametrize("N,K", SHAPES)
+def test_parity_quantized_normal(cuda, G, O, name, N, K):
+    t = G.CLAIMED[name]
+    W = normal_weights(N, K, seed=1000 + N + K)
+    raw = O.quantize(t, W)
+    x = normal_x(K, seed=7 + K)
+    y = gemv_gpu(cuda, G, t, raw, N, K, x)
+    check_parity(y, O.gemv(t, raw, N, K, x), f"{name} {N}x{K}")
+
+
+@pytest.mark.parametrize("name", TYPES)
+def test_parity_random_blocks(cuda, G, O, name):
+    t = G.CLAIMED[name]
+    N, K = 96, 1024
+    raw = random_blocks(t, N, K, seed=101)
+    x = np.random.default_rng(42).uniform(-0.5, 0.5, K).astype(np.float32)
+    y = gemv_gpu(cuda, G, t, raw, N, K, x)
+    check_parity(y, O.gemv(t, raw, N, K, x), name)
+
+
+@pytest.mark.parametrize("name", TYPES)
+def test_zero_activations_give_exact_zero(cuda, G, O, name):
+    # tests/test-gemv-accuracy.cpp:184-217 and tests/test-kquants-gemv.cpp:262-270
+    t = G.CLAIMED[name]
+    N, K = 40, 512
+    raw = random_blocks(t, N, K, seed=505)
+    y = gemv_gpu(cuda, G, t, raw, N, K, np.zeros(K, np.float32))
+    assert np.all(y == 0.0)
+
+
+@pytest.mark.parametrize("N,K", [(1, 32), (1, 4096), (33, 64), (127, 128), (255, 64), (384, 128),
+                                 (513, 64), (1536, 128), (256, 256), (1024, 1024)])
+def test_q4_0_boundary_shapes(cuda, G, O, N, K):
+    # tests/test-gemv-accuracy.cpp:322-371
+    raw = random_blocks(G.Q4_0, N, K, seed=810)
+    x = np.random.default_rng(811).uniform(-1, 1, K).astype(np.float32)
+    y = gemv_gpu(cuda, G, G.Q4_0, raw, N, K, x)
+    check_parity(y, O.gemv(G.Q4_0, raw, N, K, x), f"Q4_0 {N}x{K}")
+
+
+@pytest.mark.parametrize("N,K", [(4096, 4096), (11008, 4096)])
+def test_q4_0_model_shapes(cuda, G, O, N, K):
+    # tests/test-gemv-accuracy.cpp:373-396
+    raw = random_blocks(G.Q4_0, N, K, seed=820)
+    x = np.random.default_rng(821).uniform(-1, 1, K).astype(np.float32)
+    y = gemv_gpu(cuda, G, G.Q4_0, raw, N, K, x)
+    check_parity(y, O.gemv(G.Q4_0, raw, N, K, x), f"Q4_0 {N}x{K}")
+
+
+@pytest.mark.parametrize("name", TYPES)
+@pytest.mark.parametrize("N,K", [(11008, 2048), (2048, 11008)])
+def test_sweep_shapes_config2(cuda, G, O, name, N, K):
+    # BASELINE.json configs[2] shapes, synthetic N(0, 0.02) weights, N(0, 1) x
+    t = G.CLAIMED[name]
+    if t == G.Q4_0:
+        pytest.skip("configs[2] is the K-quant / IQ sweep")
+    raw = O.quantize(t, normal_weights(N, K, seed=31))
+    x = normal_x(K, seed=32)
+    y = gemv_gpu(cuda, G, t, raw, N, K, x)
+    check_parity(y, O.gemv(t, raw, N, K, x), f"{name} {N}x{K}")
+
+
+def test_quantizers_match_oracle(cuda, G, O):
+    for t in (G.Q4_0, G.Q4_K):
+        N, K = 64, 2048
+        W = normal_weights(N, K, seed=77)
+        d_w = to_dev(cuda, W)
+        d_q = cuda.empty(N * G.row_bytes(t, K), dtype=cuda.uint8, device="cuda")
+        G.check(G.lib().b200_quantize(t, d_w.data_ptr(), d_q.data_ptr(), N, K, 0), "quantize")
+        cuda.cuda.synchronize()
+        assert np.array_equal(d_q.cpu().numpy(), O.quantize(t, W)), G.TYPE_NAME[t]
+
+
+def test_fill_normal_statistics(cuda, G):
+    n = 1 << 20
+    d = cuda.empty(n, dtype=cuda.float32, device="cuda")
+    G.check(G.lib().b200_fill_normal(d.data_ptr(), n, 123, 0.02, 0), "fill_normal")
+    a = d.cpu().numpy()
+    assert np.isfinite(a).all()
+    assert abs(a.mean()) < 1e-4 and abs(a.std() - 0.02) < 2e-4
+
+
+def test_bf16_activation_path(cuda, G, O):
+    # reference run_bf16 (src/xdna-gemv-engine.cpp:1894-1908), checked against gemv_bf16
+    N, K = 512, 256
+    raw = random_blocks(G.Q4_0, N, K, seed=303)
+    xb = O.f32_to_bf16(np.random.default_rng(404).uniform(-1, 1, K).astype(np.float32))
+    d_xb = to_dev(cuda, xb)
+    d_x = cuda.empty(K, dtype=cuda.float32, device="cuda")
+    G.check(G.lib().b200_bf16_to_f32(d_xb.data_ptr(), d_x.data_ptr(), K, 0), "bf16")
+    cuda.cuda.synchronize()
+    x = d_x.cpu().numpy()
+    assert np.array_equal(x.view(np.uint32) >> 16, xb.astype(np.uint32))
+    y = gemv_gpu(cuda, G, G.Q4_0, raw, N, K, x)
+    check_parity(y, O.gemv_q4_0_bf16(raw, N, K, xb), "bf16")
+
+
+def test_launcher_rejects_bad_shapes(cuda, G):
+    L = G.lib()
+    d = cuda.zeros(1024, dtype=cuda.float32, device="cuda")
+    assert L.b200_gemv(G.Q4_0, d.data_ptr(), d.data_ptr(), d.data_ptr(), 10, 33, 0, 0) != 0
+    assert L.b200_gemv(G.Q4_K, d.data_ptr(), d.data_ptr(), d.data_ptr(), 10, 5121, 0, 0) != 0
+    assert L.b200_gemv(7, d.data_ptr(), d.data_ptr(), d.data_ptr(), 10, 256, 0, 0) != 0
+    assert L.b200_gemv(G.Q4_0, d.data_ptr(), d.data_ptr() + 4, d.data_ptr(), 10, 256, 0, 0) != 0
+
+
+# ------------------------------------------------------------------ compat ABI
+def _np_ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def test_compute_graph_known_answer(cuda, G):
+    # tests/test-backend.cpp:59-97: N=128, K=256, qs=0x99, d=1, x=0.5 -> 128.0
+    N, K = 128, 256
+    blk = np.zeros((N * K // 32, 18), np.uint8)
+    blk[:, 0], blk[:, 1] = 0x00, 0x3C
+    blk[:, 2:] = 0x99
+    w_data = blk.reshape(-1).copy()
+    x_data = np.full(K, 0.5, np.float32)
+    y_data = np.zeros(N, np.float32)
+    w = G.tensor(G.Q4_0, [K, N, 1, 1], data=_np_ptr(w_data))
+    x = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(x_data))
+    node = G.mul_mat_node(w, x, _np_ptr(y_data), N)
+    with G.Backend(0) as be:
+        assert G.lib().ggml_backend_is_xdna(be.h)
+        assert be.compute([node])
+    assert np.all(np.abs(y_data - 128.0) < 1e-3)
+
+
+def test_compute_graph_host_and_device_operands(cuda, G, O):
+    N, K = 256, 2048
+    t = G.Q4_K
+    raw = O.quantize(t, normal_weights(N, K, seed=5))
+    x = normal_x(K, seed=6)
+    y_ref = O.gemv(t, raw, N, K, x)
+    with G.Backend(0) as be:
+        # (a) everything in host memory: weights uploaded per call
+        y = np.zeros(N, np.float32)
+        w = G.tensor(t, [K, N, 1, 1], data=_np_ptr(raw))
+        xt = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(x))
+        assert be.compute([G.mul_mat_node(w, xt, _np_ptr(y), N)])
+        check_parity(y, y_ref, "host operands")
+        # (b) weights resident in a B200 buffer, x / y in device memory
+        buf = G.Buffer(raw.nbytes + 8192, dev=0)
+        wd = buf.alloc(G.tensor(t, [K, N, 1, 1]))
+        buf.set(wd, _np_ptr(raw), 0, raw.nbytes)
+        d_x = to_dev(cuda, x)
+        d_y = cuda.zeros(N, dtype=cuda.float32, device="cuda")
+        xt2 = G.tensor(G.F32, [K, 1, 1, 1], data=d_x.data_ptr())
+        assert be.compute([G.mul_mat_node(wd, xt2, d_y.data_ptr(), N)])
+        check_parity(d_y.cpu().numpy(), y_ref, "device operands")
+        # (c) resident weights, host x / y
+        y2 = np.zeros(N, np.float32)
+        assert be.compute([G.mul_mat_node(wd, xt, _np_ptr(y2), N)])
+        check_parity(y2, y_ref, "resident weights, host activations")
+        buf.free()
+
+
+def test_compute_graph_chained_host_nodes(cuda, G, O):
+    # node 2 consumes node 1's host output inside one compute_graph call
+    t = G.Q4_0
+    K = N = 512
+    r1 = O.quantize(t, normal_weights(N, K, seed=1))
+    r2 = O.quantize(t, normal_weights(N, K, seed=2))
+    x = normal_x(K, seed=3)
+    h = np.zeros(N, np.float32)
+    y = np.zeros(N, np.float32)
+    w1 = G.tensor(t, [K, N, 1, 1], data=_np_ptr(r1))
+    w2 = G.tensor(t, [K, N, 1, 1], data=_np_ptr(r2))
+    xt = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(x))
+    ht = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(h))
+    n1 = G.mul_mat_node(w1, xt, _np_ptr(h), N)
+    n2 = G.mul_mat_node(w2, ht, _np_ptr(y), N)
+    with G.Backend(0) as be:
+        assert be.compute([n1, n2])
+    h_ref = O.gemv(t, r1, N, K, x)
+    check_parity(h, h_ref, "node 1")
+    check_parity(y, O.gemv(t, r2, N, K, h), "node 2 (consumes node 1)")
+
+
+def test_compute_graph_rejects_bad_nodes(cuda, G):
+    K, N = 5121, 64
+    w_data = np.zeros(64 * 1024, np.uint8)
+    x_data = np.zeros(K, np.float32)
+    y_data = np.zeros(N, np.float32)
+    w = G.tensor(G.Q4_K, [K, N, 1, 1], data=_np_ptr(w_data))
+    x = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(x_data))
+    with G.Backend(0) as be:
+        assert not be.compute([G.mul_mat_node(w, x, _np_ptr(y_data), N)])
+        w.type = G.F32  # unsupported weight type
+        w.ne[0] = 256
+        assert not be.compute([G.mul_mat_node(w, x, _np_ptr(y_data), N)])
+
+
+def test_buffer_roundtrip_and_partial_writes(cuda, G, O):
+    rng = np.random.default_rng(9)
+    for name in TYPES:
+        t = G.CLAIMED[name]
+        N, K = 37, 512
+        raw = random_blocks(t, N, K, seed=11)
+        buf = G.Buffer(2 * raw.nbytes + 8192, dev=0)
+        wt = buf.alloc(G.tensor(t, [K, N, 1, 1]))
+        buf.set(wt, _np_ptr(raw), 0, raw.nbytes)
+        back = np.zeros_like(raw)
+        buf.get(wt, _np_ptr(back), 0, raw.nbytes)
+        assert np.array_equal(back, raw), name
+        # partial, unaligned write and read
+        patch = rng.integers(0, 256, 333, dtype=np.uint8)
+        off = 1111
+        buf.set(wt, _np_ptr(patch), off, patch.size)
+        raw2 = raw.copy()
+        raw2[off:off + patch.size] = patch
+        part = np.zeros(500, np.uint8)
+        buf.get(wt, _np_ptr(part), 1000, 500)
+        assert np.array_equal(part, raw2[1000:1500]), name
+        buf.get(wt, _np_ptr(back), 0, raw.nbytes)
+        assert np.array_equal(back, raw2), name
+        # memset and clear act on the GGUF view
+        buf.memset(wt, 0x5A, 100, 700)
+        raw2[100:800] = 0x5A
+        buf.get(wt, _np_ptr(back), 0, raw.nbytes)
+        assert np.array_equal(back, raw2), name
+        buf.clear(0x33)
+        buf.get(wt, _np_ptr(back), 0, raw.nbytes)
+        assert np.all(back == 0x33), name
+        buf.free()
+
+
+def test_concurrent_threads_share_a_backend(cuda, G, O):
+    # tests/test-gemv-accuracy.cpp:529-621: 4 threads x iterations, no races,
+    # no cross-contamination between threads' activations
+    N, K = 512, 256
+    raw = random_blocks(G.Q4_0, N, K, seed=9999)
+    expected = [O.gemv(G.Q4_0, raw, N, K, np.full(K, t + 1.0, np.float32)) for t in range(4)]
+    errors = []
+    with G.Backend(0) as be:
+        def worker(tid):
+            x = np.full(K, tid + 1.0, np.float32)
+            y = np.zeros(N, np.float32)
+            w = G.tensor(G.Q4_0, [K, N, 1, 1], data=_np_ptr(raw))
+            xt = G.tensor(G.F32, [K, 1, 1, 1], data=_np_ptr(x))
+            node = G.mul_mat_node(w, xt, _np_ptr(y), N)
+            for _ in range(20):
+                y[:] = 0
+                if not be.compute([node]):
+                    errors.append("compute failed")
+                    return
+                s = np.abs(y - expected[tid]).max()
+                if s > 1e-3 * max(1.0, np.abs(expected[tid]).max()):
+                    errors.append(f"thread {tid}: maxabs {s}")
+
+        th = [threading.Thread(target=worker, args=(i,)) for i in range(4)]
+        [x.start() for x in th]
+        [x.join() for x in th]
+    assert not errors, errors[:4]

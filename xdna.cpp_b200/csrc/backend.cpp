@@ -1,0 +1,1076 @@
+// Host runtime of the B200 decode-GEMV backend: the compat C ABI, HBM buffer
+// types with a bounded pinned upload path, and the MUL_MAT graph executor.
+//
+// Reference counterparts:
+//   src/ggml-xdna.cpp:95-147    supports_op_impl      -> supports_mul_mat()
+//   src/ggml-xdna.cpp:149-308   process_mul_mat_node  -> plan_node()/run_jobs()
+//   src/ggml-xdna.cpp:316-470   buffer / buffer-type  -> Buffer, BufferType
+//   src/ggml-xdna.cpp:719-844   compat entry points   -> extern "C" section
+//   src/dma_streamer.cpp:153-419 bounded 2-slot pinned staging -> Staging
+//
+// Compute is synchronous per call, as in the reference (caps.async = false):
+// activations and outputs may be host or device pointers; host ones go
+// through a pinned bounce arena on the backend's stream and outputs are
+// written back before compute_graph returns.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ggml-b200.h"
+#include "formats.cuh"
+#include "gemv.cuh"
+
+namespace xb {
+
+// ------------------------------------------------------------------ errors
+namespace {
+thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    fprintf(stderr, "[b200 error] %s\n", buf);
+}
+
+bool cuda_ok(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return true;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+constexpr uint32_t kBackendMagic = 0x58444E41;  // "XDNA", reference src/ggml-xdna.cpp:32
+constexpr uint32_t kBufferMagic = 0x58425546;   // "XBUF"
+constexpr uint32_t kBuftMagic = 0x58425454;     // "XBTT"
+constexpr size_t kAlignment = 4096;             // reference buft_get_alignment :407-410
+
+int device_count() {
+    static int count = -1;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        count = n;
+    });
+    return count;
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && prev != cur) cudaSetDevice(prev);
+    }
+};
+
+size_t env_size(const char* name, size_t dflt) {
+    const char* v = getenv(name);
+    if (!v || !*v) return dflt;
+    const long long x = atoll(v);
+    return x > 0 ? static_cast<size_t>(x) : dflt;
+}
+
+size_t type_size_bytes(int type, int64_t* blck) {
+    // ggml block sizes for the types a buffer may hold (reference :427-448)
+    *blck = 1;
+    switch (type) {
+        case GGML_TYPE_F32: case GGML_TYPE_I32: return 4;
+        case GGML_TYPE_F16: case GGML_TYPE_BF16: case GGML_TYPE_I16: return 2;
+        case GGML_TYPE_I8: return 1;
+        case GGML_TYPE_I64: case GGML_TYPE_F64: return 8;
+        case GGML_TYPE_Q4_1: *blck = 32; return 20;
+        case GGML_TYPE_Q5_0: *blck = 32; return 22;
+        case GGML_TYPE_Q5_1: *blck = 32; return 24;
+        case GGML_TYPE_Q8_0: *blck = 32; return 34;
+        default: {
+            const FormatInfo f = format_info(type);
+            if (f.block_vals) {
+                *blck = f.block_vals;
+                return static_cast<size_t>(f.block_bytes);
+            }
+            return 4;
+        }
+    }
+}
+
+size_t tensor_nbytes(const ggml_tensor_xdna* t) {
+    int64_t blck = 1;
+    const size_t ts = type_size_bytes(t->type, &blck);
+    const int64_t ne0 = t->ne[0] > 0 ? t->ne[0] : 1;
+    const int64_t ne1 = t->ne[1] > 0 ? t->ne[1] : 1;
+    const int64_t ne2 = t->ne[2] > 0 ? t->ne[2] : 1;
+    const int64_t ne3 = t->ne[3] > 0 ? t->ne[3] : 1;
+    return static_cast<size_t>(ne0 / blck) * ts * static_cast<size_t>(ne1 * ne2 * ne3);
+}
+
+// ------------------------------------------------------------------ staging
+// Bounded pinned upload/download path of one device: two pinned host slots and
+// two device slots (slot size XDNA_B200_STAGING_MB, default 64 MiB), used
+// round-robin with an event per slot -- the B200 analogue of the reference's
+// 2 x 128 MiB staging ring (src/dma_streamer.cpp:165-172).
+struct Staging {
+    int dev = 0;
+    size_t slot_bytes = 0;
+    void* pinned[2] = {nullptr, nullptr};
+    void* devbuf[2] = {nullptr, nullptr};
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    cudaStream_t stream = nullptr;
+    int next = 0;
+    std::mutex mtx;
+    bool ready = false;
+
+    bool init(int d) {
+        if (ready) return true;
+        dev = d;
+        DeviceGuard g(dev);
+        slot_bytes = env_size("XDNA_B200_STAGING_MB", 64) << 20;
+        if (!cuda_ok(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "staging stream")) return false;
+        for (int s = 0; s < 2; ++s) {
+            if (!cuda_ok(cudaHostAlloc(&pinned[s], slot_bytes, cudaHostAllocPortable), "staging pinned alloc"))
+                return false;
+            if (!cuda_ok(cudaMalloc(&devbuf[s], slot_bytes), "staging device alloc")) return false;
+            if (!cuda_ok(cudaEventCreateWithFlags(&done[s], cudaEventDisableTiming), "staging event")) return false;
+        }
+        ready = true;
+        return true;
+    }
+    int acquire() {  // a free slot (its previous work finished)
+        const int s = next;
+        next ^= 1;
+        cudaEventSynchronize(done[s]);
+        return s;
+    }
+};
+
+Staging& staging_for(int dev) {
+    static std::mutex m;
+    static std::map<int, std::unique_ptr<Staging>> all;
+    std::lock_guard<std::mutex> lk(m);
+    auto& p = all[dev];
+    if (!p) p = std::make_unique<Staging>();
+    return *p;
+}
+
+// ------------------------------------------------------------------ objects
+struct BufferType {
+    uint32_t magic = kBuftMagic;
+    int dev = 0;
+    bool host = false;
+};
+
+struct TensorInfo {
+    int type = 0;
+    int64_t K = 0, N = 0, nmat = 1;
+    size_t mat_bytes = 0;
+    bool packed = false;  // stripe layout (claimed quant type)
+};
+
+struct Buffer {
+    uint32_t magic = kBufferMagic;
+    BufferType* buft = nullptr;
+    void* base = nullptr;
+    size_t size = 0;
+    bool owned = true;
+    std::mutex mtx;
+    std::map<uintptr_t, TensorInfo> tensors;  // keyed by tensor data address
+};
+
+struct BufferRegistry {
+    std::mutex mtx;
+    std::map<uintptr_t, Buffer*> by_base;
+    void add(Buffer* b) {
+        std::lock_guard<std::mutex> lk(mtx);
+        by_base[reinterpret_cast<uintptr_t>(b->base)] = b;
+    }
+    void remove(Buffer* b) {
+        std::lock_guard<std::mutex> lk(mtx);
+        by_base.erase(reinterpret_cast<uintptr_t>(b->base));
+    }
+    Buffer* find(const void* p) {
+        std::lock_guard<std::mutex> lk(mtx);
+        const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+        auto it = by_base.upper_bound(a);
+        if (it == by_base.begin()) return nullptr;
+        --it;
+        Buffer* b = it->second;
+        return (a >= it->first && a < it->first + std::max<size_t>(b->size, 1)) ? b : nullptr;
+    }
+};
+BufferRegistry& registry() {
+    static BufferRegistry r;
+    return r;
+}
+
+BufferType* buft_instance(int dev, bool host) {
+    static std::mutex m;
+    static std::map<std::pair<int, bool>, std::unique_ptr<BufferType>> all;
+    std::lock_guard<std::mutex> lk(m);
+    auto& p = all[{dev, host}];
+    if (!p) {
+        p = std::make_unique<BufferType>();
+        p->dev = dev;
+        p->host = host;
+    }
+    return p.get();
+}
+
+BufferType* as_buft(void* p) {
+    auto* b = static_cast<BufferType*>(p);
+    return (b && b->magic == kBuftMagic) ? b : nullptr;
+}
+Buffer* as_buffer(void* p) {
+    auto* b = static_cast<Buffer*>(p);
+    return (b && b->magic == kBufferMagic) ? b : nullptr;
+}
+
+// Grow-only device / pinned arenas with bump allocation, reset when the
+// stream has drained.
+struct Arena {
+    bool pinned = false;
+    void* base = nullptr;
+    size_t cap = 0, used = 0;
+    void release() {
+        if (base) pinned ? cudaFreeHost(base) : cudaFree(base);
+        base = nullptr;
+        cap = used = 0;
+    }
+    bool reserve(size_t bytes) {  // only when used == 0
+        if (bytes <= cap) return true;
+        release();
+        size_t c = 1 << 20;
+        while (c < bytes) c <<= 1;
+        const cudaError_t e = pinned ? cudaHostAlloc(&base, c, cudaHostAllocPortable) : cudaMalloc(&base, c);
+        if (e != cudaSuccess) {
+            base = nullptr;
+            return cuda_ok(e, pinned ? "pinned arena alloc" : "device arena alloc");
+        }
+        cap = c;
+        return true;
+    }
+    void* take(size_t bytes) {
+        const size_t off = (used + 255) & ~size_t(255);
+        if (off + bytes > cap) return nullptr;
+        used = off + bytes;
+        return static_cast<char*>(base) + off;
+    }
+};
+
+struct Backend {
+    uint32_t magic = kBackendMagic;
+    int dev = 0;
+    cudaStream_t stream = nullptr;
+    std::mutex mtx;
+    Arena dev_arena{false}, host_arena{true};
+    // host weight matrices uploaded for the current call (see run_jobs)
+    Arena wt_arena{false};
+    struct PendingOut {
+        void* dst;
+        const void* src;
+        size_t bytes;
+    };
+    std::vector<PendingOut> pending;
+};
+
+Backend* as_backend(void* p) {
+    auto* b = static_cast<Backend*>(p);
+    return (b && b->magic == kBackendMagic) ? b : nullptr;
+}
+
+bool is_device_pointer(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// --------------------------------------------------------- tensor transfers
+// A tensor of a claimed quant type is held as nmat matrices of N rows, each in
+// the stripe layout.  Transfers walk tile-aligned row chunks of at most one
+// staging slot.
+struct Chunk {
+    int64_t mat, row0, nrows;
+    size_t byte0, bytes;  // tensor-relative GGUF byte range of the chunk
+};
+
+std::vector<Chunk> chunks_for(const TensorInfo& ti, size_t off, size_t size, size_t slot_bytes) {
+    std::vector<Chunk> out;
+    const size_t rb = static_cast<size_t>(ti.mat_bytes / std::max<int64_t>(ti.N, 1));
+    if (rb == 0 || size == 0) return out;
+    const int64_t tile_rows_per_chunk =
+        std::max<int64_t>(TILE_ROWS, static_cast<int64_t>(slot_bytes / (rb * TILE_ROWS)) * TILE_ROWS);
+    const size_t end = off + size;
+    for (int64_t m = off / ti.mat_bytes; m < ti.nmat && static_cast<size_t>(m) * ti.mat_bytes < end; ++m) {
+        const size_t mb = static_cast<size_t>(m) * ti.mat_bytes;
+        const size_t lo = std::max(off, mb) - mb, hi = std::min(end, mb + ti.mat_bytes) - mb;
+        int64_t r0 = static_cast<int64_t>(lo / rb) / TILE_ROWS * TILE_ROWS;
+        const int64_t r1 = static_cast<int64_t>((hi + rb - 1) / rb);
+        while (r0 < r1) {
+            const int64_t n = std::min<int64_t>(tile_rows_per_chunk, ti.N - r0);
+            out.push_back({m, r0, n, mb + static_cast<size_t>(r0) * rb, static_cast<size_t>(n) * rb});
+            r0 += n;
+        }
+    }
+    return out;
+}
+
+bool upload_packed(Staging& st, const TensorInfo& ti, uint8_t* dev_tensor, const uint8_t* host, size_t off,
+                   size_t size, const uint8_t* fill /* memset value or null */) {
+    for (const Chunk& c : chunks_for(ti, off, size, st.slot_bytes)) {
+        const int s = st.acquire();
+        uint8_t* raw = static_cast<uint8_t*>(st.devbuf[s]);
+        uint8_t* dst = dev_tensor + c.byte0;
+        const size_t w0 = std::max(off, c.byte0), w1 = std::min(off + size, c.byte0 + c.bytes);
+        const bool full = (w0 == c.byte0 && w1 == c.byte0 + c.bytes);
+        if (!full) {  // read-modify-write: bring the chunk back to GGUF layout first
+            if (!cuda_ok(unpack_launch(ti.type, dst, raw, ti.N, ti.K, c.row0, c.nrows, st.stream), "unpack"))
+                return false;
+        }
+        if (fill) {
+            if (!cuda_ok(cudaMemsetAsync(raw + (w0 - c.byte0), *fill, w1 - w0, st.stream), "memset")) return false;
+        } else {
+            memcpy(st.pinned[s], host + (w0 - off), w1 - w0);
+            if (!cuda_ok(cudaMemcpyAsync(raw + (w0 - c.byte0), st.pinned[s], w1 - w0, cudaMemcpyHostToDevice,
+                                         st.stream),
+                         "H2D"))
+                return false;
+        }
+        if (!cuda_ok(repack_launch(ti.type, raw, dst, ti.N, ti.K, c.row0, c.nrows, st.stream), "repack"))
+            return false;
+        cudaEventRecord(st.done[s], st.stream);
+    }
+    return cuda_ok(cudaStreamSynchronize(st.stream), "staging sync");
+}
+
+bool download_packed(Staging& st, const TensorInfo& ti, const uint8_t* dev_tensor, uint8_t* host, size_t off,
+                     size_t size) {
+    for (const Chunk& c : chunks_for(ti, off, size, st.slot_bytes)) {
+        const int s = st.acquire();
+        uint8_t* raw = static_cast<uint8_t*>(st.devbuf[s]);
+        if (!cuda_ok(unpack_launch(ti.type, dev_tensor + c.byte0, raw, ti.N, ti.K, c.row0, c.nrows, st.stream),
+                     "unpack"))
+            return false;
+        const size_t r0 = std::max(off, c.byte0), r1 = std::min(off + size, c.byte0 + c.bytes);
+        if (!cuda_ok(cudaMemcpyAsync(st.pinned[s], raw + (r0 - c.byte0), r1 - r0, cudaMemcpyDeviceToHost, st.stream),
+                     "D2H"))
+            return false;
+        if (!cuda_ok(cudaStreamSynchronize(st.stream), "staging sync")) return false;
+        memcpy(host + (r0 - off), st.pinned[s], r1 - r0);
+        cudaEventRecord(st.done[s], st.stream);
+    }
+    return true;
+}
+
+bool copy_plain(Staging& st, void* dev, const void* host_src, void* host_dst, size_t size) {
+    for (size_t o = 0; o < size; o += st.slot_bytes) {
+        const size_t n = std::min(st.slot_bytes, size - o);
+        const int s = st.acquire();
+        if (host_src) {
+            memcpy(st.pinned[s], static_cast<const char*>(host_src) + o, n);
+            if (!cuda_ok(cudaMemcpyAsync(static_cast<char*>(dev) + o, st.pinned[s], n, cudaMemcpyHostToDevice,
+                                         st.stream),
+                         "H2D"))
+                return false;
+            cudaEventRecord(st.done[s], st.stream);
+        } else {
+            if (!cuda_ok(cudaMemcpyAsync(st.pinned[s], static_cast<char*>(dev) + o, n, cudaMemcpyDeviceToHost,
+                                         st.stream),
+                         "D2H"))
+                return false;
+            if (!cuda_ok(cudaStreamSynchronize(st.stream), "staging sync")) return false;
+            memcpy(static_cast<char*>(host_dst) + o, st.pinned[s], n);
+            cudaEventRecord(st.done[s], st.stream);
+        }
+    }
+    return cuda_ok(cudaStreamSynchronize(st.stream), "staging sync");
+}
+
+// Describe (and validate) a tensor written into a device buffer.
+bool tensor_info_for(const ggml_tensor_xdna* t, TensorInfo* ti) {
+    ti->type = t->type;
+    ti->K = t->ne[0];
+    ti->N = t->ne[1] > 0 ? t->ne[1] : 1;
+    ti->nmat = (t->ne[2] > 0 ? t->ne[2] : 1) * (t->ne[3] > 0 ? t->ne[3] : 1);
+    const FormatInfo f = format_info(t->type);
+    const bool contiguous =
+        (t->nb[1] == 0 || t->nb[1] == static_cast<size_t>(ti->K / std::max(f.block_vals, 1)) * f.block_bytes);
+    ti->packed = f.block_vals != 0 && ti->K > 0 && ti->K % f.block_vals == 0 && contiguous;
+    ti->mat_bytes = ti->packed ? static_cast<size_t>(ti->N) * static_cast<size_t>(ti->K / f.block_vals) * f.block_bytes
+                               : 0;
+    return true;
+}
+
+// ------------------------------------------------------------- supports_op
+bool row_bytes_for(int type, int64_t K, size_t* rb) {
+    const FormatInfo f = format_info(type);
+    if (!f.block_vals || K % f.block_vals) return false;
+    *rb = static_cast<size_t>(K / f.block_vals) * f.block_bytes;
+    return true;
+}
+
+// Same predicate as the reference's supports_op_impl (src/ggml-xdna.cpp:95-147)
+// for the compat ABI, where the loader-probe relaxation never applies: MUL_MAT,
+// F32 src1, M == 1, N >= 32, N % 4 == 0, K a block multiple, packed rows.
+bool supports_mul_mat(const ggml_tensor_xdna* op) {
+    if (!op || op->op != GGML_OP_MUL_MAT) return false;
+    const ggml_tensor_xdna* src0 = op->src[0];
+    const ggml_tensor_xdna* src1 = op->src[1];
+    if (!src0 || !src1) return false;
+    if (src1->type != GGML_TYPE_F32) return false;
+    const int64_t K = src0->ne[0], N = src0->ne[1], M = src1->ne[1];
+    if (M != 1 || N < 32 || N % 4 != 0) return false;
+    size_t rb = 0;
+    if (!type_supported(src0->type) || !row_bytes_for(src0->type, K, &rb)) return false;
+    return src0->nb[1] == 0 || src0->nb[1] == rb;
+}
+
+// ------------------------------------------------------------- execution
+struct Job {
+    int type;
+    const void* w;  // device, stripe layout
+    const float* x; // device, 16-byte aligned
+    float* y;       // device
+    int64_t N, K;
+};
+
+bool ranges_overlap(const void* a, size_t an, const void* b, size_t bn) {
+    const char* pa = static_cast<const char*>(a);
+    const char* pb = static_cast<const char*>(b);
+    return pa < pb + bn && pb < pa + an;
+}
+
+bool flush(Backend* be) {
+    if (!cuda_ok(cudaStreamSynchronize(be->stream), "compute sync")) {
+        be->pending.clear();
+        be->dev_arena.used = be->host_arena.used = be->wt_arena.used = 0;
+        return false;
+    }
+    for (const auto& p : be->pending) memcpy(p.dst, p.src, p.bytes);
+    be->pending.clear();
+    be->dev_arena.used = be->host_arena.used = be->wt_arena.used = 0;
+    return true;
+}
+
+bool overlaps_pending(Backend* be, const void* p, size_t n) {
+    for (const auto& o : be->pending)
+        if (ranges_overlap(o.dst, o.bytes, p, n)) return true;
+    return false;
+}
+
+// device copy of a host range (through the pinned arena), 256-byte aligned
+const void* stage_in(Backend* be, const void* host, size_t bytes) {
+    if (overlaps_pending(be, host, bytes) && !flush(be)) return nullptr;
+    void* h = be->host_arena.take(bytes);
+    void* d = be->dev_arena.take(bytes);
+    if (!h || !d) {
+        if (!flush(be)) return nullptr;
+        if (!be->host_arena.reserve(std::max(bytes, be->host_arena.cap * 2)) ||
+            !be->dev_arena.reserve(std::max(bytes, be->dev_arena.cap * 2)))
+            return nullptr;
+        h = be->host_arena.take(bytes);
+        d = be->dev_arena.take(bytes);
+        if (!h || !d) return nullptr;
+    }
+    memcpy(h, host, bytes);
+    if (!cuda_ok(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, be->stream), "H2D activations")) return nullptr;
+    return d;
+}
+
+// device output slot for a host destination, written back at flush time
+float* stage_out(Backend* be, void* host, size_t bytes, void** pinned_out) {
+    void* h = be->host_arena.take(bytes);
+    void* d = be->dev_arena.take(bytes);
+    if (!h || !d) {
+        if (!flush(be)) return nullptr;
+        if (!be->host_arena.reserve(std::max(bytes, be->host_arena.cap * 2)) ||
+            !be->dev_arena.reserve(std::max(bytes, be->dev_arena.cap * 2)))
+            return nullptr;
+        h = be->host_arena.take(bytes);
+        d = be->dev_arena.take(bytes);
+        if (!h || !d) return nullptr;
+    }
+    *pinned_out = h;
+    (void)host;
+    return static_cast<float*>(d);
+}
+
+// Host-resident weights: uploaded and repacked for this call into the weight
+// arena (there is no residency cache keyed by host pointer: a caller may
+// rewrite the same host memory between calls).  Device-resident weights
+// belong in a buffer of ggml_backend_xdna_buffer_type().
+const void* stage_weights(Backend* be, int type, const uint8_t* host, int64_t N, int64_t K, size_t rb) {
+    const size_t bytes = static_cast<size_t>(N) * rb;
+    if (overlaps_pending(be, host, bytes) && !flush(be)) return nullptr;
+    void* d = be->wt_arena.take(bytes);
+    if (!d) {
+        if (!flush(be)) return nullptr;
+        if (!be->wt_arena.reserve(std::max(bytes, be->wt_arena.cap * 2))) return nullptr;
+        d = be->wt_arena.take(bytes);
+        if (!d) return nullptr;
+    }
+    Staging& st = staging_for(be->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(be->dev)) return nullptr;
+    TensorInfo ti;
+    ti.type = type;
+    ti.K = K;
+    ti.N = N;
+    ti.nmat = 1;
+    ti.mat_bytes = bytes;
+    ti.packed = true;
+    // the staging stream must not overwrite d while an earlier kernel of this
+    // call still reads the arena region: make the staging stream wait.
+    cudaEvent_t ev;
+    cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    cudaEventRecord(ev, be->stream);
+    cudaStreamWaitEvent(st.stream, ev, 0);
+    cudaEventDestroy(ev);
+    if (!upload_packed(st, ti, static_cast<uint8_t*>(d), host, 0, bytes, nullptr)) return nullptr;
+    return d;
+}
+
+// One MUL_MAT node -> jobs (reference process_mul_mat_node, :149-308).
+bool run_node(Backend* be, ggml_tensor_xdna* node) {
+    ggml_tensor_xdna* src0 = node->src[0];
+    ggml_tensor_xdna* src1 = node->src[1];
+    const char* name = node->name;
+    if (!src0 || !src1) {
+        set_error("node '%s' missing src0/src1", name);
+        return false;
+    }
+    if (src1->type != GGML_TYPE_F32) {
+        set_error("node '%s' src1 type %d != F32", name, src1->type);
+        return false;
+    }
+    if (!node->data || !src0->data || !src1->data) {
+        set_error("node '%s' null data ptrs: node->data=%p src0->data=%p src1->data=%p", name, node->data,
+                  src0->data, src1->data);
+        return false;
+    }
+    const int64_t K = src0->ne[0], N = src0->ne[1], M = src1->ne[1];
+    if (M == 0 || N == 0) return true;
+    if (M < 0 || N < 0 || K < 0) {
+        set_error("node '%s' negative dim: M=%ld N=%ld K=%ld", name, long(M), long(N), long(K));
+        return false;
+    }
+    const FormatInfo f = format_info(src0->type);
+    if (!f.block_vals) {
+        set_error("node '%s' unsupported src0 type=%d", name, src0->type);
+        return false;
+    }
+    if (K % f.block_vals != 0) {
+        set_error("node '%s' K=%ld not div by %d", name, long(K), f.block_vals);
+        return false;
+    }
+    const size_t rb = static_cast<size_t>(K / f.block_vals) * f.block_bytes;
+    if (src0->nb[1] != 0 && src0->nb[1] != rb) {
+        set_error("node '%s' src0 nb1 mismatch: %zu != %zu", name, src0->nb[1], rb);
+        return false;
+    }
+    const size_t total_weight_bytes = static_cast<size_t>(N) * rb;
+    const int64_t ne2 = node->ne[2] > 0 ? node->ne[2] : 1;
+    const int64_t ne3 = node->ne[3] > 0 ? node->ne[3] : 1;
+    const size_t dst_stride1 = node->nb[1] > 0 ? node->nb[1] : static_cast<size_t>(N) * sizeof(float);
+    const size_t dst_stride2 = node->nb[2] > 0 ? node->nb[2] : dst_stride1 * M;
+    const size_t dst_stride3 = node->nb[3] > 0 ? node->nb[3] : dst_stride2 * ne2;
+    const size_t src1_stride1 = src1->nb[1] > 0 ? src1->nb[1] : static_cast<size_t>(K) * sizeof(float);
+    const size_t src1_stride2 = src1->ne[2] > 1 ? (src1->nb[2] > 0 ? src1->nb[2] : src1_stride1 * M) : 0;
+    const size_t src1_stride3 = src1->ne[3] > 1 ? (src1->nb[3] > 0 ? src1->nb[3] : src1_stride2 * ne2) : 0;
+    const size_t src0_stride2 = src0->ne[2] > 1 ? (src0->nb[2] > 0 ? src0->nb[2] : total_weight_bytes) : 0;
+    const size_t src0_stride3 = src0->ne[3] > 1 ? (src0->nb[3] > 0 ? src0->nb[3] : src0_stride2 * ne2) : 0;
+
+    // where the weights live
+    Buffer* wbuf = registry().find(src0->data);
+    const TensorInfo* wti = nullptr;
+    if (wbuf && !wbuf->buft->host) {
+        std::lock_guard<std::mutex> lk(wbuf->mtx);
+        auto it = wbuf->tensors.find(reinterpret_cast<uintptr_t>(src0->data));
+        if (it == wbuf->tensors.end() || !it->second.packed) {
+            set_error("node '%s': weights in a B200 buffer were not written with "
+                      "ggml_backend_xdna_buffer_set_tensor as a claimed quant type",
+                      name);
+            return false;
+        }
+        wti = &it->second;
+        if (wbuf->buft->dev != be->dev) {
+            set_error("node '%s': weights live on device %d, backend is on device %d", name, wbuf->buft->dev, be->dev);
+            return false;
+        }
+    }
+    const bool w_device = wbuf != nullptr && !wbuf->buft->host;
+    const bool x_device = is_device_pointer(src1->data);
+    const bool y_device = is_device_pointer(node->data);
+
+    const uint8_t* base_w = static_cast<const uint8_t*>(src0->data);
+    const char* base_x = static_cast<const char*>(src1->data);
+    char* base_y = static_cast<char*>(node->data);
+
+    for (int64_t i3 = 0; i3 < ne3; ++i3) {
+        for (int64_t i2 = 0; i2 < ne2; ++i2) {
+            const uint8_t* w_host = base_w + i3 * src0_stride3 + i2 * src0_stride2;
+            const void* w_dev = nullptr;
+            if (w_device) {
+                const size_t rel = static_cast<size_t>(w_host - base_w);
+                if (wti->mat_bytes == 0 || rel % wti->mat_bytes != 0 || wti->K != K || wti->N != N) {
+                    set_error("node '%s': weight slice does not match the packed tensor geometry", name);
+                    return false;
+                }
+                w_dev = w_host;
+            } else {
+                w_dev = stage_weights(be, src0->type, w_host, N, K, rb);
+                if (!w_dev) {
+                    set_error("node '%s': weight upload failed: %s", name, g_last_error.c_str());
+                    return false;
+                }
+            }
+            for (int64_t m = 0; m < M; ++m) {
+                const char* a_m = base_x + i3 * src1_stride3 + i2 * src1_stride2 + m * src1_stride1;
+                char* o_m = base_y + i3 * dst_stride3 + i2 * dst_stride2 + m * dst_stride1;
+                const float* xd;
+                if (x_device && (reinterpret_cast<uintptr_t>(a_m) & 15u) == 0) {
+                    xd = reinterpret_cast<const float*>(a_m);
+                } else if (x_device) {
+                    void* d = be->dev_arena.take(static_cast<size_t>(K) * 4);
+                    if (!d) {
+                        if (!flush(be) || !be->dev_arena.reserve(std::max<size_t>(K * 4, be->dev_arena.cap * 2)))
+                            return false;
+                        d = be->dev_arena.take(static_cast<size_t>(K) * 4);
+                    }
+                    if (!cuda_ok(cudaMemcpyAsync(d, a_m, static_cast<size_t>(K) * 4, cudaMemcpyDeviceToDevice,
+                                                 be->stream),
+                                 "align activations"))
+                        return false;
+                    xd = static_cast<const float*>(d);
+                } else {
+                    xd = static_cast<const float*>(stage_in(be, a_m, static_cast<size_t>(K) * 4));
+                    if (!xd) return false;
+                }
+                float* yd;
+                void* pinned = nullptr;
+                if (y_device) {
+                    yd = reinterpret_cast<float*>(o_m);
+                } else {
+                    yd = stage_out(be, o_m, static_cast<size_t>(N) * 4, &pinned);
+                    if (!yd) return false;
+                }
+                LaunchOpts lo;
+                if (!cuda_ok(gemv_launch(src0->type, w_dev, xd, yd, N, K, be->stream, lo), "gemv launch"))
+                    return false;
+                if (!y_device) {
+                    if (!cuda_ok(cudaMemcpyAsync(pinned, yd, static_cast<size_t>(N) * 4, cudaMemcpyDeviceToHost,
+                                                 be->stream),
+                                 "D2H outputs"))
+                        return false;
+                    be->pending.push_back({o_m, pinned, static_cast<size_t>(N) * 4});
+                }
+            }
+        }
+    }
+    return true;
+}
+
+}  // namespace
+}  // namespace xb
+
+using namespace xb;
+
+// ====================================================================== C ABI
+extern "C" {
+
+const char* ggml_backend_xdna_last_error(void) { return g_last_error.c_str(); }
+
+size_t ggml_backend_xdna_get_device_count(void) { return static_cast<size_t>(device_count()); }
+
+void ggml_backend_xdna_get_device_memory(size_t dev_num, size_t* free_bytes, size_t* total_bytes) {
+    size_t f = 0, t = 0;
+    if (static_cast<int>(dev_num) < device_count()) {
+        DeviceGuard g(static_cast<int>(dev_num));
+        if (cudaMemGetInfo(&f, &t) != cudaSuccess) cudaGetLastError();
+    }
+    if (free_bytes) *free_bytes = f;
+    if (total_bytes) *total_bytes = t;
+}
+
+ggml_backend_reg_t ggml_backend_xdna_reg(void) {
+    static uint32_t reg_token = 0x58524547;  // "XREG": opaque registry handle of the compat ABI
+    return &reg_token;
+}
+
+ggml_backend_t ggml_backend_xdna_init(size_t dev_num) {
+    if (static_cast<int>(dev_num) >= device_count()) {
+        set_error("ggml_backend_xdna_init: CUDA device %zu not available (%d device(s))", dev_num, device_count());
+        return nullptr;
+    }
+    auto be = std::make_unique<Backend>();
+    be->dev = static_cast<int>(dev_num);
+    DeviceGuard g(be->dev);
+    if (!cuda_ok(cudaStreamCreateWithFlags(&be->stream, cudaStreamNonBlocking), "backend stream")) return nullptr;
+    return be.release();
+}
+
+bool ggml_backend_is_xdna(ggml_backend_t backend) { return as_backend(backend) != nullptr; }
+
+void ggml_backend_xdna_free(ggml_backend_t backend) {
+    Backend* be = as_backend(backend);
+    if (!be) return;
+    {
+        DeviceGuard g(be->dev);
+        std::lock_guard<std::mutex> lk(be->mtx);
+        cudaStreamSynchronize(be->stream);
+        be->dev_arena.release();
+        be->host_arena.release();
+        be->wt_arena.release();
+        cudaStreamDestroy(be->stream);
+        be->magic = 0;
+    }
+    delete be;
+}
+
+void ggml_backend_xdna_synchronize(ggml_backend_t backend) {
+    Backend* be = as_backend(backend);
+    if (!be) return;
+    DeviceGuard g(be->dev);
+    cudaStreamSynchronize(be->stream);
+}
+
+ggml_backend_buffer_type_t ggml_backend_xdna_buffer_type(size_t dev_num) {
+    return buft_instance(static_cast<int>(dev_num), false);
+}
+
+ggml_backend_buffer_type_t ggml_backend_xdna_host_buffer_type(void) { return buft_instance(0, true); }
+
+bool ggml_backend_xdna_supports_op(ggml_backend_t backend, const struct ggml_tensor_xdna* op) {
+    (void)backend;
+    return supports_mul_mat(op);
+}
+
+bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_xdna** nodes, size_t n_nodes) {
+    if (!backend || !nodes || n_nodes == 0) return false;
+    Backend* be = as_backend(backend);
+    if (!be) return false;
+    std::lock_guard<std::mutex> lk(be->mtx);
+    DeviceGuard g(be->dev);
+    static const bool trace = getenv("XDNA_TRACE_NODES") != nullptr;
+    bool ok = true;
+    for (size_t i = 0; i < n_nodes && ok; ++i) {
+        ggml_tensor_xdna* node = nodes[i];
+        if (!node || node->op != GGML_OP_MUL_MAT) continue;
+        ok = run_node(be, node);
+        if (trace && ok && node->src[0])
+            fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued\n", i,
+                    node->name[0] ? node->name : "unnamed", node->src[0]->type, long(node->src[0]->ne[1]),
+                    long(node->src[0]->ne[0]));
+    }
+    const bool flushed = flush(be);
+    return ok && flushed;
+}
+
+// ---------------------------------------------------------------- buffers
+const char* ggml_backend_xdna_buft_name(ggml_backend_buffer_type_t buft) {
+    BufferType* t = as_buft(buft);
+    return !t ? "" : (t->host ? "B200_Host" : "B200");
+}
+
+size_t ggml_backend_xdna_buft_get_alignment(ggml_backend_buffer_type_t buft) {
+    (void)buft;
+    return kAlignment;
+}
+
+size_t ggml_backend_xdna_buft_get_alloc_size(ggml_backend_buffer_type_t buft, const struct ggml_tensor_xdna* tensor) {
+    (void)buft;
+    return tensor ? tensor_nbytes(tensor) : 0;
+}
+
+bool ggml_backend_xdna_buft_is_host(ggml_backend_buffer_type_t buft) {
+    BufferType* t = as_buft(buft);
+    return t && t->host;
+}
+
+ggml_backend_buffer_t ggml_backend_xdna_buft_alloc_buffer(ggml_backend_buffer_type_t buft, size_t size) {
+    BufferType* t = as_buft(buft);
+    if (!t) {
+        set_error("alloc_buffer: not a B200 buffer type");
+        return nullptr;
+    }
+    if (!t->host && t->dev >= device_count()) {
+        set_error("alloc_buffer: CUDA device %d not available", t->dev);
+        return nullptr;
+    }
+    auto b = std::make_unique<Buffer>();
+    b->buft = t;
+    b->size = size;
+    const size_t alloc = size == 0 ? kAlignment : size;
+    DeviceGuard g(t->host ? 0 : t->dev);
+    const cudaError_t e =
+        t->host ? cudaHostAlloc(&b->base, alloc, cudaHostAllocPortable) : cudaMalloc(&b->base, alloc);
+    if (e != cudaSuccess) {
+        set_error("alloc_buffer(%zu bytes): %s", size, cudaGetErrorString(e));
+        cudaGetLastError();
+        return nullptr;
+    }
+    registry().add(b.get());
+    return b.release();
+}
+
+void ggml_backend_xdna_buffer_free(ggml_backend_buffer_t buffer) {
+    Buffer* b = as_buffer(buffer);
+    if (!b) return;
+    registry().remove(b);
+    if (b->owned && b->base) {
+        DeviceGuard g(b->buft->host ? 0 : b->buft->dev);
+        b->buft->host ? cudaFreeHost(b->base) : cudaFree(b->base);
+    }
+    b->magic = 0;
+    delete b;
+}
+
+void* ggml_backend_xdna_buffer_get_base(ggml_backend_buffer_t buffer) {
+    Buffer* b = as_buffer(buffer);
+    return b ? b->base : nullptr;
+}
+
+size_t ggml_backend_xdna_buffer_get_size(ggml_backend_buffer_t buffer) {
+    Buffer* b = as_buffer(buffer);
+    return b ? b->size : 0;
+}
+
+static bool check_tensor_range(Buffer* b, const ggml_tensor_xdna* t, size_t offset, size_t size, const char* what) {
+    if (!b || !t || !t->data) {
+        set_error("%s: null buffer/tensor", what);
+        return false;
+    }
+    const char* base = static_cast<const char*>(b->base);
+    const char* d = static_cast<const char*>(t->data);
+    const size_t nbytes = tensor_nbytes(t);
+    if (d < base || d + nbytes > base + b->size) {
+        set_error("%s: tensor '%s' [%p, +%zu) is not inside the buffer", what, t->name, t->data, nbytes);
+        return false;
+    }
+    if (offset > nbytes || size > nbytes - offset) {
+        set_error("%s: range [%zu, +%zu) exceeds tensor '%s' size %zu", what, offset, size, t->name, nbytes);
+        return false;
+    }
+    return true;
+}
+
+bool ggml_backend_xdna_buffer_set_tensor(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna* tensor,
+                                         const void* data, size_t offset, size_t size) {
+    Buffer* b = as_buffer(buffer);
+    if (!check_tensor_range(b, tensor, offset, size, "set_tensor")) return false;
+    if (size == 0) return true;
+    if (!data) {
+        set_error("set_tensor: null data");
+        return false;
+    }
+    if (b->buft->host) {
+        memcpy(static_cast<char*>(tensor->data) + offset, data, size);
+        return true;
+    }
+    TensorInfo ti;
+    tensor_info_for(tensor, &ti);
+    {
+        std::lock_guard<std::mutex> lk(b->mtx);
+        b->tensors[reinterpret_cast<uintptr_t>(tensor->data)] = ti;
+    }
+    Staging& st = staging_for(b->buft->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(b->buft->dev)) return false;
+    DeviceGuard g(b->buft->dev);
+    if (ti.packed)
+        return upload_packed(st, ti, static_cast<uint8_t*>(tensor->data), static_cast<const uint8_t*>(data), offset,
+                             size, nullptr);
+    return copy_plain(st, static_cast<char*>(tensor->data) + offset, data, nullptr, size);
+}
+
+bool ggml_backend_xdna_buffer_get_tensor(ggml_backend_buffer_t buffer, const struct ggml_tensor_xdna* tensor,
+                                         void* data, size_t offset, size_t size) {
+    Buffer* b = as_buffer(buffer);
+    if (!check_tensor_range(b, tensor, offset, size, "get_tensor")) return false;
+    if (size == 0) return true;
+    if (!data) {
+        set_error("get_tensor: null data");
+        return false;
+    }
+    if (b->buft->host) {
+        memcpy(data, static_cast<const char*>(tensor->data) + offset, size);
+        return true;
+    }
+    TensorInfo ti;
+    bool known = false;
+    {
+        std::lock_guard<std::mutex> lk(b->mtx);
+        auto it = b->tensors.find(reinterpret_cast<uintptr_t>(tensor->data));
+        if (it != b->tensors.end()) {
+            ti = it->second;
+            known = true;
+        }
+    }
+    Staging& st = staging_for(b->buft->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(b->buft->dev)) return false;
+    DeviceGuard g(b->buft->dev);
+    if (known && ti.packed)
+        return download_packed(st, ti, static_cast<const uint8_t*>(tensor->data), static_cast<uint8_t*>(data), offset,
+                               size);
+    return copy_plain(st, static_cast<char*>(tensor->data) + offset, nullptr, data, size);
+}
+
+bool ggml_backend_xdna_buffer_memset_tensor(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna* tensor,
+                                            uint8_t value, size_t offset, size_t size) {
+    Buffer* b = as_buffer(buffer);
+    if (!check_tensor_range(b, tensor, offset, size, "memset_tensor")) return false;
+    if (size == 0) return true;
+    if (b->buft->host) {
+        memset(static_cast<char*>(tensor->data) + offset, value, size);
+        return true;
+    }
+    TensorInfo ti;
+    tensor_info_for(tensor, &ti);
+    {
+        std::lock_guard<std::mutex> lk(b->mtx);
+        b->tensors[reinterpret_cast<uintptr_t>(tensor->data)] = ti;
+    }
+    Staging& st = staging_for(b->buft->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(b->buft->dev)) return false;
+    DeviceGuard g(b->buft->dev);
+    if (ti.packed)
+        return upload_packed(st, ti, static_cast<uint8_t*>(tensor->data), nullptr, offset, size, &value);
+    if (!cuda_ok(cudaMemsetAsync(static_cast<char*>(tensor->data) + offset, value, size, st.stream), "memset"))
+        return false;
+    return cuda_ok(cudaStreamSynchronize(st.stream), "memset sync");
+}
+
+bool ggml_backend_xdna_buffer_clear(ggml_backend_buffer_t buffer, uint8_t value) {
+    Buffer* b = as_buffer(buffer);
+    if (!b) return false;
+    if (b->buft->host) {
+        if (b->size) memset(b->base, value, b->size);
+        return true;
+    }
+    DeviceGuard g(b->buft->dev);
+    if (b->size && !cuda_ok(cudaMemset(b->base, value, b->size), "clear")) return false;
+    // Every byte of the GGUF view is now `value`; stripe tiles whose repack
+    // transposes bit planes (Q5_K qh, Q3_K hmask) need the transposed value.
+    std::vector<std::pair<uintptr_t, TensorInfo>> fix;
+    {
+        std::lock_guard<std::mutex> lk(b->mtx);
+        for (auto& kv : b->tensors)
+            if (kv.second.packed && (kv.second.type == T_Q5_K || kv.second.type == T_Q3_K)) fix.push_back(kv);
+    }
+    if (fix.empty()) return true;
+    Staging& st = staging_for(b->buft->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(b->buft->dev)) return false;
+    for (auto& kv : fix)
+        if (!upload_packed(st, kv.second, reinterpret_cast<uint8_t*>(kv.first), nullptr, 0,
+                           kv.second.mat_bytes * kv.second.nmat, &value))
+            return false;
+    return true;
+}
+
+// ---------------------------------------------------------------- launcher
+static int launch_rc(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return 0;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return -static_cast<int>(e);
+}
+
+int b200_gemv(int type, const void* w_packed, const float* x, float* y, int64_t n, int64_t k, void* stream,
+              int pdl) {
+    const FormatInfo f = format_info(type);
+    if (!f.block_vals || k < 0 || k % f.block_vals || n < 0) {
+        set_error("b200_gemv: bad type %d / shape N=%ld K=%ld", type, long(n), long(k));
+        return -1;
+    }
+    if (n > 0 && (!w_packed || !x || !y)) {
+        set_error("b200_gemv: null pointer");
+        return -1;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15u) {
+        set_error("b200_gemv: x must be 16-byte aligned");
+        return -1;
+    }
+    LaunchOpts lo;
+    lo.pdl = pdl != 0;
+    return launch_rc(gemv_launch(type, w_packed, x, y, n, k, static_cast<cudaStream_t>(stream), lo), "b200_gemv");
+}
+
+int b200_repack(int type, const void* raw, void* packed, int64_t n, int64_t k, void* stream) {
+    return launch_rc(repack_launch(type, raw, packed, n, k, 0, n, static_cast<cudaStream_t>(stream)), "b200_repack");
+}
+
+int b200_unpack(int type, const void* packed, void* raw, int64_t n, int64_t k, void* stream) {
+    return launch_rc(unpack_launch(type, packed, raw, n, k, 0, n, static_cast<cudaStream_t>(stream)), "b200_unpack");
+}
+
+int b200_bf16_to_f32(const uint16_t* src, float* dst, int64_t n, void* stream) {
+    return launch_rc(bf16_to_f32_launch(src, dst, n, static_cast<cudaStream_t>(stream)), "b200_bf16_to_f32");
+}
+
+int b200_fill_normal(float* out, int64_t n, uint64_t seed, float sigma, void* stream) {
+    return launch_rc(fill_normal_launch(out, n, seed, sigma, static_cast<cudaStream_t>(stream)), "b200_fill_normal");
+}
+
+int b200_quantize(int type, const float* src, void* dst, int64_t n, int64_t k, void* stream) {
+    return launch_rc(quantize_launch(type, src, dst, n, k, static_cast<cudaStream_t>(stream)), "b200_quantize");
+}
+
+static int host_repack(int type, const void* src, void* dst, int64_t n, int64_t k, bool pack) {
+    const FormatInfo f = format_info(type);
+    if (!f.block_vals || k < 0 || k % f.block_vals || n < 0 || (n > 0 && (!src || !dst))) {
+        set_error("b200_%s_host: bad arguments", pack ? "repack" : "unpack");
+        return -1;
+    }
+    const Geometry g = make_geometry(type, n, k);
+    for (int64_t t = 0; t < g.ntiles; ++t) {
+        const int tr = static_cast<int>(std::min<int64_t>(TILE_ROWS, n - t * TILE_ROWS));
+        const size_t base = static_cast<size_t>(t) * TILE_ROWS * g.row_bytes;
+        for (int r = 0; r < tr; ++r)
+            for (int64_t b = 0; b < g.nb; ++b) {
+                if (pack)
+                    repack_one(g, tr, r, b, static_cast<const uint8_t*>(src) + base, static_cast<uint8_t*>(dst) + base);
+                else
+                    unrepack_one(g, tr, r, b, static_cast<const uint8_t*>(src) + base, static_cast<uint8_t*>(dst) + base);
+            }
+    }
+    return 0;
+}
+
+int b200_repack_host(int type, const void* raw, void* packed, int64_t n, int64_t k) {
+    return host_repack(type, raw, packed, n, k, true);
+}
+
+int b200_unpack_host(int type, const void* packed, void* raw, int64_t n, int64_t k) {
+    return host_repack(type, packed, raw, n, k, false);
+}
+
+size_t b200_row_bytes(int type, int64_t k) {
+    size_t rb = 0;
+    return (k >= 0 && row_bytes_for(type, k, &rb)) ? rb : 0;
+}
+
+size_t b200_gemv_smem_bytes(int type, int64_t k) { return gemv_smem_bytes(type, k); }
+
+}  // extern "C"

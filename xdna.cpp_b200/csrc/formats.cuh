@@ -1,0 +1,328 @@
+// Weight formats of the decode-GEMV path and the B200 "stripe tile" layout.
+//
+// GGUF block formats (byte layouts, reference include/xdna/kquants.h:50-160 and
+// include/xdna/q4_0_reference.h:11-35; IQ3_XXS / IQ2_S as gguf 0.19.0
+// gguf/quants.py:901-1056) are split, per tile of TILE_ROWS rows, into three
+// regions so the GEMV kernel can stream them with 16-byte loads:
+//
+//   payload : quant bits, in 16-byte pieces ordered [piece][row][unit]  so the
+//             32 lanes of a warp, each owning one "unit" of a row, read 512
+//             contiguous bytes per load instruction;
+//   aux     : per-block sub-scale records (A bytes), ordered [row][block];
+//   d       : per-block fp16 super-scales (D bytes), ordered [row][block].
+//
+// A unit is UNIT_VALS consecutive values of a row (32 for Q4_0, 128 = half a
+// super-block otherwise).  The tile occupies exactly rows * row_bytes bytes,
+// the same span as the GGUF rows it holds, so the repack is an in-place
+// permutation of each tile and tensor offsets/sizes are unchanged.
+// Q5_K's qh and Q3_K's hmask bit planes are transposed during the repack into
+// per-unit 16-byte pieces (see pack_block); every other byte moves unchanged.
+// Scales are kept bit-exact (fp16 / 6-bit / int8), unlike the reference's
+// lossy BF16 column prepack (src/xdna-q4-prepack.cpp:564-600).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define XB_HD __host__ __device__ __forceinline__
+#else
+#define XB_HD inline
+#endif
+
+namespace xb {
+
+// ggml type ids (reference include/xdna/ggml-xdna.h:19-48)
+enum : int {
+    T_Q4_0 = 2, T_Q3_K = 11, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14,
+    T_IQ3_XXS = 18, T_IQ3_S = 21, T_IQ2_S = 22, T_IQ4_XS = 23,
+};
+
+// Rows per stripe tile.  Eight rows make every tile start on a 16-byte
+// boundary for all nine formats (8 x an even block size is a multiple of 16),
+// which the kernels' 16-byte loads require.
+constexpr int TILE_ROWS = 8;
+
+struct FormatInfo {
+    int type;
+    int block_vals;   // values per GGUF block
+    int block_bytes;  // bytes per GGUF block
+    int unit_vals;    // values per GEMV unit
+    int pieces;       // 16-byte payload pieces per unit
+    int a_bytes;      // aux record bytes per block
+    int d_bytes;      // d record bytes per block
+};
+
+XB_HD FormatInfo format_info(int type) {
+    switch (type) {
+        //                   type       bv   bb  uv  pc  a   d
+        case T_Q4_0:    return {T_Q4_0,    32,  18, 32,  1, 0,  2};
+        case T_Q4_K:    return {T_Q4_K,   256, 144, 128, 4, 12, 4};
+        case T_Q5_K:    return {T_Q5_K,   256, 176, 128, 5, 12, 4};
+        case T_Q3_K:    return {T_Q3_K,   256, 110, 128, 3, 12, 2};
+        case T_Q6_K:    return {T_Q6_K,   256, 210, 128, 6, 16, 2};
+        case T_IQ4_XS:  return {T_IQ4_XS, 256, 136, 128, 4, 4,  4};
+        case T_IQ3_S:   return {T_IQ3_S,  256, 110, 128, 3, 12, 2};
+        case T_IQ3_XXS: return {T_IQ3_XXS,256,  98, 128, 3, 0,  2};
+        case T_IQ2_S:   return {T_IQ2_S,  256,  82, 128, 2, 16, 2};
+        default:        return {0, 0, 0, 0, 0, 0, 0};
+    }
+}
+
+XB_HD bool type_supported(int type) { return format_info(type).block_vals != 0; }
+
+// Geometry of one weight matrix [N rows x K values].
+struct Geometry {
+    FormatInfo f;
+    int64_t N, K;
+    int64_t nb;         // blocks per row
+    int64_t nu;         // units per row
+    int64_t row_bytes;  // GGUF bytes per row
+    int64_t ntiles;
+};
+
+XB_HD Geometry make_geometry(int type, int64_t N, int64_t K) {
+    Geometry g;
+    g.f = format_info(type);
+    g.N = N;
+    g.K = K;
+    g.nb = g.f.block_vals ? K / g.f.block_vals : 0;
+    g.nu = g.f.unit_vals ? K / g.f.unit_vals : 0;
+    g.row_bytes = g.nb * g.f.block_bytes;
+    g.ntiles = (N + TILE_ROWS - 1) / TILE_ROWS;
+    return g;
+}
+
+// Byte offsets inside a tile holding `tr` rows.
+XB_HD int64_t tile_payload_off(const Geometry& g, int tr, int piece, int row, int64_t unit) {
+    return ((int64_t(piece) * tr + row) * g.nu + unit) * 16;
+}
+XB_HD int64_t tile_aux_off(const Geometry& g, int tr, int row, int64_t block) {
+    return int64_t(g.f.pieces) * tr * g.nu * 16 + (int64_t(row) * g.nb + block) * g.f.a_bytes;
+}
+XB_HD int64_t tile_d_off(const Geometry& g, int tr, int row, int64_t block) {
+    return int64_t(g.f.pieces) * tr * g.nu * 16 + int64_t(tr) * g.nb * g.f.a_bytes +
+           (int64_t(row) * g.nb + block) * g.f.d_bytes;
+}
+
+// ---------------------------------------------------------------------------
+// Per-block repack.  `blk` is one GGUF block; the unit pieces, aux and d
+// records it produces are written through the three output pointers:
+//   pieces[u][p] (u < units per block), aux (a_bytes), d (d_bytes).
+// unpack_block is the exact inverse.
+// ---------------------------------------------------------------------------
+
+// Bit (8*i + k) of word jj of the transposed plane = bit `bit` of src[4*k + i]
+// (k: 4-byte word index 0..7 within a 32-byte group, i: byte within word).
+XB_HD uint32_t transpose_plane(const uint8_t* src32, int bit) {
+    uint32_t w = 0;
+    for (int k = 0; k < 8; ++k)
+        for (int i = 0; i < 4; ++i)
+            w |= uint32_t((src32[4 * k + i] >> bit) & 1u) << (8 * i + k);
+    return w;
+}
+
+XB_HD void untranspose_plane(uint32_t w, uint8_t* dst32, int bit) {
+    for (int k = 0; k < 8; ++k)
+        for (int i = 0; i < 4; ++i)
+            dst32[4 * k + i] = uint8_t(dst32[4 * k + i] | (((w >> (8 * i + k)) & 1u) << bit));
+}
+
+XB_HD void put32(uint8_t* p, uint32_t v) {
+    p[0] = uint8_t(v); p[1] = uint8_t(v >> 8); p[2] = uint8_t(v >> 16); p[3] = uint8_t(v >> 24);
+}
+XB_HD uint32_t get32(const uint8_t* p) {
+    return uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16) | (uint32_t(p[3]) << 24);
+}
+XB_HD void copy_bytes(uint8_t* dst, const uint8_t* src, int n) {
+    for (int i = 0; i < n; ++i) dst[i] = src[i];
+}
+
+// pieces: array of (units per block) * pieces * 16 bytes, unit-major.
+XB_HD void pack_block(int type, const uint8_t* blk, uint8_t* pieces, uint8_t* aux, uint8_t* d) {
+    switch (type) {
+        case T_Q4_0:  // d(2) qs(16)
+            copy_bytes(d, blk, 2);
+            copy_bytes(pieces, blk + 2, 16);
+            break;
+        case T_Q4_K:  // d dmin(4) scales(12) qs(128)
+            copy_bytes(d, blk, 4);
+            copy_bytes(aux, blk + 4, 12);
+            for (int h = 0; h < 2; ++h) copy_bytes(pieces + h * 64, blk + 16 + 64 * h, 64);
+            break;
+        case T_Q5_K:  // d dmin(4) scales(12) qh(32) qs(128)
+            copy_bytes(d, blk, 4);
+            copy_bytes(aux, blk + 4, 12);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 80;
+                copy_bytes(u, blk + 48 + 64 * h, 64);
+                for (int jj = 0; jj < 2; ++jj)
+                    for (int n = 0; n < 2; ++n)
+                        put32(u + 64 + 4 * (2 * jj + n), transpose_plane(blk + 16, 2 * (2 * h + jj) + n));
+            }
+            break;
+        case T_Q3_K:  // hmask(32) qs(64) scales(12) d(2)
+            copy_bytes(d, blk + 108, 2);
+            copy_bytes(aux, blk + 96, 12);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 48;
+                copy_bytes(u, blk + 32 + 32 * h, 32);
+                for (int j2 = 0; j2 < 4; ++j2) put32(u + 32 + 4 * j2, transpose_plane(blk, 4 * h + j2));
+            }
+            break;
+        case T_Q6_K:  // ql(128) qh(64) scales(16) d(2)
+            copy_bytes(d, blk + 208, 2);
+            copy_bytes(aux, blk + 192, 16);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 96;
+                copy_bytes(u, blk + 64 * h, 64);
+                copy_bytes(u + 64, blk + 128 + 32 * h, 32);
+            }
+            break;
+        case T_IQ4_XS:  // d(2) scales_h(2) scales_l(4) qs(128)
+            copy_bytes(d, blk, 4);
+            copy_bytes(aux, blk + 4, 4);
+            for (int h = 0; h < 2; ++h) copy_bytes(pieces + h * 64, blk + 8 + 64 * h, 64);
+            break;
+        case T_IQ3_S:  // d(2) qs(64) qh(8) signs(32) scales(4)
+            copy_bytes(d, blk, 2);
+            copy_bytes(aux, blk + 66, 8);
+            copy_bytes(aux + 8, blk + 106, 4);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 48;
+                copy_bytes(u, blk + 2 + 32 * h, 32);
+                copy_bytes(u + 32, blk + 74 + 16 * h, 16);
+            }
+            break;
+        case T_IQ3_XXS:  // d(2) qs(64) scales_signs(32)
+            copy_bytes(d, blk, 2);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 48;
+                copy_bytes(u, blk + 2 + 32 * h, 32);
+                copy_bytes(u + 32, blk + 66 + 16 * h, 16);
+            }
+            break;
+        case T_IQ2_S:  // d(2) qs(32) signs(32) qh(8) scales(8)
+            copy_bytes(d, blk, 2);
+            copy_bytes(aux, blk + 66, 16);
+            for (int h = 0; h < 2; ++h) {
+                uint8_t* u = pieces + h * 32;
+                copy_bytes(u, blk + 2 + 16 * h, 16);
+                copy_bytes(u + 16, blk + 34 + 16 * h, 16);
+            }
+            break;
+        default:
+            break;
+    }
+}
+
+XB_HD void unpack_block(int type, const uint8_t* pieces, const uint8_t* aux, const uint8_t* d, uint8_t* blk) {
+    switch (type) {
+        case T_Q4_0:
+            copy_bytes(blk, d, 2);
+            copy_bytes(blk + 2, pieces, 16);
+            break;
+        case T_Q4_K:
+            copy_bytes(blk, d, 4);
+            copy_bytes(blk + 4, aux, 12);
+            for (int h = 0; h < 2; ++h) copy_bytes(blk + 16 + 64 * h, pieces + h * 64, 64);
+            break;
+        case T_Q5_K:
+            copy_bytes(blk, d, 4);
+            copy_bytes(blk + 4, aux, 12);
+            for (int i = 0; i < 32; ++i) blk[16 + i] = 0;
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 80;
+                copy_bytes(blk + 48 + 64 * h, u, 64);
+                for (int jj = 0; jj < 2; ++jj)
+                    for (int n = 0; n < 2; ++n)
+                        untranspose_plane(get32(u + 64 + 4 * (2 * jj + n)), blk + 16, 2 * (2 * h + jj) + n);
+            }
+            break;
+        case T_Q3_K:
+            copy_bytes(blk + 108, d, 2);
+            copy_bytes(blk + 96, aux, 12);
+            for (int i = 0; i < 32; ++i) blk[i] = 0;
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 48;
+                copy_bytes(blk + 32 + 32 * h, u, 32);
+                for (int j2 = 0; j2 < 4; ++j2) untranspose_plane(get32(u + 32 + 4 * j2), blk, 4 * h + j2);
+            }
+            break;
+        case T_Q6_K:
+            copy_bytes(blk + 208, d, 2);
+            copy_bytes(blk + 192, aux, 16);
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 96;
+                copy_bytes(blk + 64 * h, u, 64);
+                copy_bytes(blk + 128 + 32 * h, u + 64, 32);
+            }
+            break;
+        case T_IQ4_XS:
+            copy_bytes(blk, d, 4);
+            copy_bytes(blk + 4, aux, 4);
+            for (int h = 0; h < 2; ++h) copy_bytes(blk + 8 + 64 * h, pieces + h * 64, 64);
+            break;
+        case T_IQ3_S:
+            copy_bytes(blk, d, 2);
+            copy_bytes(blk + 66, aux, 8);
+            copy_bytes(blk + 106, aux + 8, 4);
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 48;
+                copy_bytes(blk + 2 + 32 * h, u, 32);
+                copy_bytes(blk + 74 + 16 * h, u + 32, 16);
+            }
+            break;
+        case T_IQ3_XXS:
+            copy_bytes(blk, d, 2);
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 48;
+                copy_bytes(blk + 2 + 32 * h, u, 32);
+                copy_bytes(blk + 66 + 16 * h, u + 32, 16);
+            }
+            break;
+        case T_IQ2_S:
+            copy_bytes(blk, d, 2);
+            copy_bytes(blk + 66, aux, 16);
+            for (int h = 0; h < 2; ++h) {
+                const uint8_t* u = pieces + h * 32;
+                copy_bytes(blk + 2 + 16 * h, u, 16);
+                copy_bytes(blk + 34 + 16 * h, u + 16, 16);
+            }
+            break;
+        default:
+            break;
+    }
+}
+
+// Repack (or unpack) one block (row r of a tile with tr rows, block b) between
+// a GGUF tile `raw` and a stripe tile `tile`.  Both point at the tile start.
+XB_HD void repack_one(const Geometry& g, int tr, int r, int64_t b, const uint8_t* raw, uint8_t* tile) {
+    const FormatInfo& f = g.f;
+    uint8_t pieces[2 * 6 * 16];
+    uint8_t aux[16];
+    uint8_t d[4];
+    pack_block(f.type, raw + r * g.row_bytes + b * f.block_bytes, pieces, aux, d);
+    const int upb = f.block_vals / f.unit_vals;
+    for (int uu = 0; uu < upb; ++uu)
+        for (int p = 0; p < f.pieces; ++p)
+            copy_bytes(tile + tile_payload_off(g, tr, p, r, b * upb + uu), pieces + (uu * f.pieces + p) * 16, 16);
+    if (f.a_bytes) copy_bytes(tile + tile_aux_off(g, tr, r, b), aux, f.a_bytes);
+    copy_bytes(tile + tile_d_off(g, tr, r, b), d, f.d_bytes);
+}
+
+XB_HD void unrepack_one(const Geometry& g, int tr, int r, int64_t b, const uint8_t* tile, uint8_t* raw) {
+    const FormatInfo& f = g.f;
+    uint8_t pieces[2 * 6 * 16];
+    uint8_t aux[16] = {0};
+    uint8_t d[4];
+    const int upb = f.block_vals / f.unit_vals;
+    for (int uu = 0; uu < upb; ++uu)
+        for (int p = 0; p < f.pieces; ++p)
+            copy_bytes(pieces + (uu * f.pieces + p) * 16, tile + tile_payload_off(g, tr, p, r, b * upb + uu), 16);
+    if (f.a_bytes) copy_bytes(aux, tile + tile_aux_off(g, tr, r, b), f.a_bytes);
+    copy_bytes(d, tile + tile_d_off(g, tr, r, b), f.d_bytes);
+    unpack_block(f.type, pieces, aux, d, raw + r * g.row_bytes + b * f.block_bytes);
+}
+
+}  // namespace xb

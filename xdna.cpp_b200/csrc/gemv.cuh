@@ -1,0 +1,36 @@
+// Internal launcher interface of the GEMV, repack and quantize kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace xb {
+
+struct LaunchOpts {
+    bool pdl = false;  // programmatic dependent launch (overlap with the previous kernel)
+};
+
+// y[N] = W[N,K] x[K]; W in the stripe-tile layout (formats.cuh), device pointers.
+cudaError_t gemv_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
+                        cudaStream_t stream, const LaunchOpts& opts);
+size_t gemv_smem_bytes(int type, int64_t K);
+
+// GGUF rows [row0, row0 + nrows) of a matrix with N rows <-> stripe tiles.
+// row0 and nrows must be tile aligned (nrows may end at N).  raw and packed
+// are device pointers to row row0 (the layouts have the same byte span).
+cudaError_t repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, int64_t row0,
+                          int64_t nrows, cudaStream_t stream);
+cudaError_t unpack_launch(int type, const void* packed, void* raw, int64_t N, int64_t K, int64_t row0,
+                          int64_t nrows, cudaStream_t stream);
+
+// BF16 activations -> F32 (reference bf16_to_float, exact).
+cudaError_t bf16_to_f32_launch(const uint16_t* src, float* dst, int64_t n, cudaStream_t stream);
+
+// Synthetic weights: N(0, sigma) F32 from a counter-based generator, and the
+// device quantisers (Q4_0: ggml quantize_row_q4_0_ref; Q4_K: this build's
+// affine 6-bit scale/min fit).  Output in GGUF layout.
+cudaError_t fill_normal_launch(float* out, int64_t n, uint64_t seed, float sigma, cudaStream_t stream);
+cudaError_t quantize_launch(int type, const float* src, void* dst, int64_t N, int64_t K, cudaStream_t stream);
+bool quantize_supported(int type);
+
+}  // namespace xb
