@@ -138,6 +138,16 @@ bool ggml_backend_xdna_buffer_get_tensor(ggml_backend_buffer_t buffer, const str
 bool ggml_backend_xdna_buffer_memset_tensor(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna *tensor,
                                             uint8_t value, size_t offset, size_t size);
 bool ggml_backend_xdna_buffer_clear(ggml_backend_buffer_t buffer, uint8_t value);
+/* Like set_tensor, with the GGUF bytes already in device memory of the same
+ * GPU (e.g. produced by a device quantiser): device-to-device, repacked in
+ * place.  No reference counterpart (its buffers are host memory). */
+bool ggml_backend_xdna_buffer_set_tensor_device(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna *tensor,
+                                                const void *dev_data, size_t offset, size_t size);
+/* Copy tensor src to dst, both in B200 buffers of one GPU, same type and shape
+ * (ggml buffer iface cpy_tensor; the reference leaves that slot empty, :370). */
+bool ggml_backend_xdna_buffer_cpy_tensor(const struct ggml_tensor_xdna *src, struct ggml_tensor_xdna *dst);
+/* The cudaStream_t the backend computes on (for event timing / interop). */
+void *ggml_backend_xdna_get_stream(ggml_backend_t backend);
 /* Wait for all work queued on the backend's stream (reference synchronize :692-694). */
 void ggml_backend_xdna_synchronize(ggml_backend_t backend);
 /* Device memory (reference dev_get_memory :505-509, which hard-codes 16 GiB). */
@@ -169,6 +179,23 @@ int b200_unpack_host(int type, const void *packed, void *raw, int64_t n, int64_t
 size_t b200_row_bytes(int type, int64_t k);
 /* Dynamic shared memory one GEMV CTA uses for row length k. */
 size_t b200_gemv_smem_bytes(int type, int64_t k);
+
+/* ============== 4. row-sharded multi-GPU execution (one process per GPU) ==============
+ * No reference counterpart: the reference drives one device.  Each rank owns
+ * rows [row0, row0 + N/world) of every weight (ggml_backend_xdna_shard_rows);
+ * a MUL_MAT node whose src0 holds the local rows and whose dst has
+ * ne[0] = N_local * world is computed locally and completed with an NCCL
+ * all-gather of the F32 slices, so every rank ends with the full output.
+ * Every rank must submit the same node sequence. */
+
+/* A fresh NCCL unique id (rank 0 creates it and distributes the 128 bytes). */
+int ggml_backend_xdna_nccl_unique_id(uint8_t out[128]);
+/* Backend of `rank` in a group of `world` ranks on device dev_num.  NCCL
+ * initialisation is bounded by XDNA_B200_NCCL_TIMEOUT_S (default 120 s);
+ * NULL on failure or timeout. */
+ggml_backend_t ggml_backend_xdna_init_sharded(size_t dev_num, int world, int rank, const uint8_t id[128]);
+/* Rows of an N-row weight owned by `rank`; N must be divisible by world. */
+int ggml_backend_xdna_shard_rows(int64_t n, int world, int rank, int64_t *row0, int64_t *nrows);
 
 #ifdef __cplusplus
 }

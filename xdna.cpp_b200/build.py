@@ -22,7 +22,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CU_SOURCES = ["gemv.cu", "repack.cu", "quantize.cu"]
 CXX_SOURCES = ["backend.cpp"]
-HEADERS = ["formats.cuh", "gemv.cuh"]
+HEADERS = ["formats.cuh", "gemv.cuh", "nccl_shim.h"]
 
 
 def _stale(target: str, deps: list[str]) -> bool:

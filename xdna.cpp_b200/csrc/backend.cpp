@@ -25,9 +25,13 @@
 #include <string>
 #include <vector>
 
+#include <chrono>
+#include <thread>
+
 #include "../../include/ggml-b200.h"
 #include "formats.cuh"
 #include "gemv.cuh"
+#include "nccl_shim.h"
 
 namespace xb {
 
@@ -279,6 +283,9 @@ struct Backend {
     uint32_t magic = kBackendMagic;
     int dev = 0;
     cudaStream_t stream = nullptr;
+    // row-sharded execution (ggml_backend_xdna_init_sharded)
+    int rank = 0, world = 1;
+    ncclComm_t comm = nullptr;
     std::mutex mtx;
     Arena dev_arena{false}, host_arena{true};
     // host weight matrices uploaded for the current call (see run_jobs)
@@ -550,6 +557,42 @@ const void* stage_weights(Backend* be, int type, const uint8_t* host, int64_t N,
     return d;
 }
 
+// ------------------------------------------------------------------ NCCL
+double nccl_timeout_s() {
+    const char* v = getenv("XDNA_B200_NCCL_TIMEOUT_S");
+    const double t = v ? atof(v) : 0.0;
+    return t > 0 ? t : 120.0;
+}
+
+// Poll a non-blocking communicator until its pending operation completes,
+// with a host-side time limit; on timeout the communicator is aborted so
+// that no rank waits forever for a peer that never arrives.
+bool nccl_wait(ncclComm_t comm, ncclResult_t r, const char* what) {
+    const NcclApi& api = nccl_api();
+    const auto t0 = std::chrono::steady_clock::now();
+    while (r == ncclInProgress) {
+        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > nccl_timeout_s()) {
+            api.CommAbort(comm);
+            set_error("%s: timed out after %.0f s (communicator aborted)", what, nccl_timeout_s());
+            return false;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (api.CommGetAsyncError(comm, &r) != ncclSuccess) break;
+    }
+    if (r != ncclSuccess) {
+        set_error("%s: %s", what, api.GetErrorString(r));
+        return false;
+    }
+    return true;
+}
+
+bool all_gather_rows(Backend* be, float* y_full, int64_t n_local) {
+    const NcclApi& api = nccl_api();
+    const ncclResult_t r = api.AllGather(y_full + be->rank * n_local, y_full, static_cast<size_t>(n_local), ncclFloat32,
+                                         be->comm, be->stream);
+    return nccl_wait(be->comm, r, "ncclAllGather");
+}
+
 // One MUL_MAT node -> jobs (reference process_mul_mat_node, :149-308).
 bool run_node(Backend* be, ggml_tensor_xdna* node) {
     ggml_tensor_xdna* src0 = node->src[0];
@@ -591,7 +634,12 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
     const size_t total_weight_bytes = static_cast<size_t>(N) * rb;
     const int64_t ne2 = node->ne[2] > 0 ? node->ne[2] : 1;
     const int64_t ne3 = node->ne[3] > 0 ? node->ne[3] : 1;
-    const size_t dst_stride1 = node->nb[1] > 0 ? node->nb[1] : static_cast<size_t>(N) * sizeof(float);
+    // Row-sharded node: src0 holds this rank's N rows of a weight with
+    // N * world rows, dst is the full output; each rank computes its slice
+    // and the slices are all-gathered over NCCL.
+    const bool sharded = be->world > 1 && node->ne[0] == N * be->world;
+    const int64_t n_out = sharded ? N * be->world : N;
+    const size_t dst_stride1 = node->nb[1] > 0 ? node->nb[1] : static_cast<size_t>(n_out) * sizeof(float);
     const size_t dst_stride2 = node->nb[2] > 0 ? node->nb[2] : dst_stride1 * M;
     const size_t dst_stride3 = node->nb[3] > 0 ? node->nb[3] : dst_stride2 * ne2;
     const size_t src1_stride1 = src1->nb[1] > 0 ? src1->nb[1] : static_cast<size_t>(K) * sizeof(float);
@@ -668,21 +716,23 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
                 }
                 float* yd;
                 void* pinned = nullptr;
+                const size_t out_bytes = static_cast<size_t>(n_out) * 4;
                 if (y_device) {
                     yd = reinterpret_cast<float*>(o_m);
                 } else {
-                    yd = stage_out(be, o_m, static_cast<size_t>(N) * 4, &pinned);
+                    yd = stage_out(be, o_m, out_bytes, &pinned);
                     if (!yd) return false;
                 }
                 LaunchOpts lo;
-                if (!cuda_ok(gemv_launch(src0->type, w_dev, xd, yd, N, K, be->stream, lo), "gemv launch"))
+                float* y_local = sharded ? yd + be->rank * N : yd;
+                if (!cuda_ok(gemv_launch(src0->type, w_dev, xd, y_local, N, K, be->stream, lo), "gemv launch"))
                     return false;
+                if (sharded && !all_gather_rows(be, yd, N)) return false;
                 if (!y_device) {
-                    if (!cuda_ok(cudaMemcpyAsync(pinned, yd, static_cast<size_t>(N) * 4, cudaMemcpyDeviceToHost,
-                                                 be->stream),
+                    if (!cuda_ok(cudaMemcpyAsync(pinned, yd, out_bytes, cudaMemcpyDeviceToHost, be->stream),
                                  "D2H outputs"))
                         return false;
-                    be->pending.push_back({o_m, pinned, static_cast<size_t>(N) * 4});
+                    be->pending.push_back({o_m, pinned, out_bytes});
                 }
             }
         }
@@ -729,6 +779,65 @@ ggml_backend_t ggml_backend_xdna_init(size_t dev_num) {
     return be.release();
 }
 
+int ggml_backend_xdna_nccl_unique_id(uint8_t out[128]) {
+    const NcclApi& api = nccl_api();
+    if (!api.ok) {
+        set_error("NCCL (libnccl.so.2) could not be loaded");
+        return -1;
+    }
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId size");
+    ncclUniqueId id;
+    const ncclResult_t r = api.GetUniqueId(&id);
+    if (r != ncclSuccess) {
+        set_error("ncclGetUniqueId: %s", api.GetErrorString(r));
+        return -2;
+    }
+    memcpy(out, &id, sizeof id);
+    return 0;
+}
+
+ggml_backend_t ggml_backend_xdna_init_sharded(size_t dev_num, int world, int rank, const uint8_t id[128]) {
+    if (world < 1 || rank < 0 || rank >= world || !id) {
+        set_error("init_sharded: bad world %d / rank %d", world, rank);
+        return nullptr;
+    }
+    Backend* be = static_cast<Backend*>(ggml_backend_xdna_init(dev_num));
+    if (!be) return nullptr;
+    be->rank = rank;
+    be->world = world;
+    if (world == 1) return be;
+    const NcclApi& api = nccl_api();
+    if (!api.ok) {
+        set_error("init_sharded: NCCL (libnccl.so.2) could not be loaded");
+        ggml_backend_xdna_free(be);
+        return nullptr;
+    }
+    DeviceGuard g(be->dev);
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof uid);
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;  // initialisation polled below with a time limit
+    const ncclResult_t r = api.CommInitRankConfig(&be->comm, world, uid, rank, &cfg);
+    if ((r != ncclSuccess && r != ncclInProgress) || !nccl_wait(be->comm, r, "ncclCommInitRankConfig")) {
+        if (r != ncclSuccess && r != ncclInProgress) set_error("ncclCommInitRankConfig: %s", api.GetErrorString(r));
+        if (be->comm && r == ncclSuccess) api.CommDestroy(be->comm);
+        be->comm = nullptr;
+        ggml_backend_xdna_free(be);
+        return nullptr;
+    }
+    return be;
+}
+
+int ggml_backend_xdna_shard_rows(int64_t n, int world, int rank, int64_t* row0, int64_t* nrows) {
+    if (world < 1 || rank < 0 || rank >= world || n < 0 || n % world != 0) {
+        set_error("shard_rows: N=%ld is not divisible by world %d", long(n), world);
+        return -1;
+    }
+    if (row0) *row0 = (n / world) * rank;
+    if (nrows) *nrows = n / world;
+    return 0;
+}
+
 bool ggml_backend_is_xdna(ggml_backend_t backend) { return as_backend(backend) != nullptr; }
 
 void ggml_backend_xdna_free(ggml_backend_t backend) {
@@ -741,10 +850,16 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         be->dev_arena.release();
         be->host_arena.release();
         be->wt_arena.release();
+        if (be->comm) nccl_api().CommDestroy(be->comm);
         cudaStreamDestroy(be->stream);
         be->magic = 0;
     }
     delete be;
+}
+
+void* ggml_backend_xdna_get_stream(ggml_backend_t backend) {
+    Backend* be = as_backend(backend);
+    return be ? static_cast<void*>(be->stream) : nullptr;
 }
 
 void ggml_backend_xdna_synchronize(ggml_backend_t backend) {
@@ -901,6 +1016,89 @@ bool ggml_backend_xdna_buffer_set_tensor(ggml_backend_buffer_t buffer, struct gg
         return upload_packed(st, ti, static_cast<uint8_t*>(tensor->data), static_cast<const uint8_t*>(data), offset,
                              size, nullptr);
     return copy_plain(st, static_cast<char*>(tensor->data) + offset, data, nullptr, size);
+}
+
+bool ggml_backend_xdna_buffer_set_tensor_device(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna* tensor,
+                                                const void* dev_data, size_t offset, size_t size) {
+    Buffer* b = as_buffer(buffer);
+    if (!check_tensor_range(b, tensor, offset, size, "set_tensor_device")) return false;
+    if (size == 0) return true;
+    if (!dev_data || b->buft->host) {
+        set_error("set_tensor_device: needs device source data and a device buffer");
+        return false;
+    }
+    TensorInfo ti;
+    tensor_info_for(tensor, &ti);
+    {
+        std::lock_guard<std::mutex> lk(b->mtx);
+        b->tensors[reinterpret_cast<uintptr_t>(tensor->data)] = ti;
+    }
+    Staging& st = staging_for(b->buft->dev);
+    std::lock_guard<std::mutex> lk(st.mtx);
+    if (!st.init(b->buft->dev)) return false;
+    DeviceGuard g(b->buft->dev);
+    uint8_t* dst = static_cast<uint8_t*>(tensor->data);
+    const uint8_t* src = static_cast<const uint8_t*>(dev_data);
+    if (!ti.packed) {
+        if (!cuda_ok(cudaMemcpyAsync(dst + offset, src, size, cudaMemcpyDeviceToDevice, st.stream), "D2D")) return false;
+        return cuda_ok(cudaStreamSynchronize(st.stream), "D2D sync");
+    }
+    for (const Chunk& c : chunks_for(ti, offset, size, st.slot_bytes)) {
+        const size_t w0 = std::max(offset, c.byte0), w1 = std::min(offset + size, c.byte0 + c.bytes);
+        if (w0 == c.byte0 && w1 == c.byte0 + c.bytes) {  // whole chunk: repack straight from the source
+            if (!cuda_ok(repack_launch(ti.type, src + (w0 - offset), dst + c.byte0, ti.N, ti.K, c.row0, c.nrows,
+                                       st.stream),
+                         "repack"))
+                return false;
+            continue;
+        }
+        const int s = st.acquire();
+        uint8_t* raw = static_cast<uint8_t*>(st.devbuf[s]);
+        if (!cuda_ok(unpack_launch(ti.type, dst + c.byte0, raw, ti.N, ti.K, c.row0, c.nrows, st.stream), "unpack") ||
+            !cuda_ok(cudaMemcpyAsync(raw + (w0 - c.byte0), src + (w0 - offset), w1 - w0, cudaMemcpyDeviceToDevice,
+                                     st.stream),
+                     "D2D") ||
+            !cuda_ok(repack_launch(ti.type, raw, dst + c.byte0, ti.N, ti.K, c.row0, c.nrows, st.stream), "repack"))
+            return false;
+        cudaEventRecord(st.done[s], st.stream);
+    }
+    return cuda_ok(cudaStreamSynchronize(st.stream), "set_tensor_device sync");
+}
+
+bool ggml_backend_xdna_buffer_cpy_tensor(const struct ggml_tensor_xdna* src, struct ggml_tensor_xdna* dst) {
+    if (!src || !dst || !src->data || !dst->data) {
+        set_error("cpy_tensor: null tensor");
+        return false;
+    }
+    Buffer* bs = registry().find(src->data);
+    Buffer* bd = registry().find(dst->data);
+    if (!bs || !bd || bs->buft->host || bd->buft->host || bs->buft->dev != bd->buft->dev) {
+        set_error("cpy_tensor: both tensors must live in B200 device buffers of one GPU");
+        return false;
+    }
+    const size_t n = tensor_nbytes(src);
+    if (src->type != dst->type || n != tensor_nbytes(dst) || src->ne[0] != dst->ne[0] || src->ne[1] != dst->ne[1]) {
+        set_error("cpy_tensor: '%s' and '%s' differ in type or shape", src->name, dst->name);
+        return false;
+    }
+    if (!check_tensor_range(bd, dst, 0, n, "cpy_tensor")) return false;
+    TensorInfo ti;
+    {
+        std::lock_guard<std::mutex> lk(bs->mtx);
+        auto it = bs->tensors.find(reinterpret_cast<uintptr_t>(src->data));
+        if (it == bs->tensors.end()) {
+            set_error("cpy_tensor: source '%s' was never written", src->name);
+            return false;
+        }
+        ti = it->second;
+    }
+    {
+        std::lock_guard<std::mutex> lk(bd->mtx);
+        bd->tensors[reinterpret_cast<uintptr_t>(dst->data)] = ti;
+    }
+    DeviceGuard g(bd->buft->dev);
+    // both tensors share the stripe layout, so the copy is byte for byte
+    return cuda_ok(cudaMemcpy(dst->data, src->data, n, cudaMemcpyDeviceToDevice), "cpy_tensor");
 }
 
 bool ggml_backend_xdna_buffer_get_tensor(ggml_backend_buffer_t buffer, const struct ggml_tensor_xdna* tensor,

@@ -23,6 +23,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "formats.cuh"
 #include "gemv.cuh"
 #include "iq_tables.h"  // generated at build time from the gguf package
@@ -36,6 +38,7 @@ constexpr int kItemRows = 4;  // rows per warp work item (x reuse factor)
 static_assert(TILE_ROWS % kItemRows == 0, "items must not straddle tiles");
 constexpr int kWarps = kThreads / 32;
 constexpr float kMagic = 8388608.0f;  // 2^23
+constexpr int kMaxDevices = 16;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -681,28 +684,56 @@ __global__ void __launch_bounds__(kThreads) gemv_tiles_kernel(const uint8_t* __r
     }
 }
 
+// Per-device launch geometry of one kernel instantiation, cached so that a
+// launch costs one cudaGetDevice plus the launch itself.
+struct LaunchCache {
+    std::mutex mtx;
+    int sms[kMaxDevices] = {};
+    size_t smem_set[kMaxDevices] = {};
+    // last few (smem bytes -> resident CTAs per SM) answers per device
+    size_t occ_smem[kMaxDevices][4] = {};
+    int occ_val[kMaxDevices][4] = {};
+    int occ_next[kMaxDevices] = {};
+};
+
 template <class D>
 cudaError_t launch_typed(const uint8_t* W, const float* x, float* y, int64_t N, int64_t K, cudaStream_t stream,
                          const LaunchOpts& opts) {
-    const Geometry g = make_geometry(D::kType, N, K);
+    static LaunchCache cache;
     const size_t smem = smem_bytes<D>(K);
-    static int s_sms = 0;
-    if (s_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&s_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (s_sms <= 0) s_sms = 148;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    int sms = 0, per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lk(cache.mtx);
+        if (cache.sms[dev] == 0) {
+            e = cudaDeviceGetAttribute(&cache.sms[dev], cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return e;
+        }
+        sms = cache.sms[dev];
+        if (smem > cache.smem_set[dev]) {
+            e = cudaFuncSetAttribute(gemv_tiles_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(smem));
+            if (e != cudaSuccess) return e;
+            cache.smem_set[dev] = smem;
+        }
+        for (int i = 0; i < 4; ++i)
+            if (cache.occ_smem[dev][i] == smem && cache.occ_val[dev][i] > 0) per_sm = cache.occ_val[dev][i];
+        if (per_sm == 0) {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tiles_kernel<D>, kThreads, smem);
+            if (e != cudaSuccess) return e;
+            if (per_sm <= 0) return cudaErrorInvalidConfiguration;
+            const int slot = cache.occ_next[dev];
+            cache.occ_next[dev] = (slot + 1) & 3;
+            cache.occ_smem[dev][slot] = smem;
+            cache.occ_val[dev][slot] = per_sm;
+        }
     }
-    cudaError_t e = cudaFuncSetAttribute(gemv_tiles_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_tiles_kernel<D>, kThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm <= 0) return cudaErrorInvalidConfiguration;
     const int64_t nitems = (N + kItemRows - 1) / kItemRows;
     int64_t blocks = (nitems + kWarps - 1) / kWarps;
-    const int64_t cap = static_cast<int64_t>(s_sms) * per_sm;
+    const int64_t cap = static_cast<int64_t>(sms) * per_sm;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
 

@@ -113,7 +113,13 @@ def lib() -> C.CDLL:
         "ggml_backend_xdna_buffer_get_tensor": (b, [vp, tp, vp, sz, sz]),
         "ggml_backend_xdna_buffer_memset_tensor": (b, [vp, tp, C.c_uint8, sz, sz]),
         "ggml_backend_xdna_buffer_clear": (b, [vp, C.c_uint8]),
+        "ggml_backend_xdna_buffer_set_tensor_device": (b, [vp, tp, vp, sz, sz]),
+        "ggml_backend_xdna_buffer_cpy_tensor": (b, [tp, tp]),
+        "ggml_backend_xdna_get_stream": (vp, [vp]),
         "ggml_backend_xdna_synchronize": (None, [vp]),
+        "ggml_backend_xdna_nccl_unique_id": (C.c_int, [C.c_char_p]),
+        "ggml_backend_xdna_init_sharded": (vp, [sz, C.c_int, C.c_int, C.c_char_p]),
+        "ggml_backend_xdna_shard_rows": (C.c_int, [i64, C.c_int, C.c_int, C.POINTER(i64), C.POINTER(i64)]),
         "ggml_backend_xdna_get_device_memory": (None, [sz, C.POINTER(sz), C.POINTER(sz)]),
         "ggml_backend_xdna_get_device_count": (sz, []),
         "b200_gemv": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, vp, C.c_int]),
@@ -144,14 +150,30 @@ def check(rc: int, what: str = "") -> None:
 
 
 # ------------------------------------------------------------------ helpers
-class Backend:
-    """RAII wrapper of a compat-ABI backend handle on one CUDA device."""
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    check(lib().ggml_backend_xdna_nccl_unique_id(buf), "nccl_unique_id")
+    return buf.raw
 
-    def __init__(self, dev: int = 0):
-        self.h = lib().ggml_backend_xdna_init(dev)
+
+def shard_rows(n: int, world: int, rank: int) -> tuple[int, int]:
+    r0, nr = C.c_int64(), C.c_int64()
+    check(lib().ggml_backend_xdna_shard_rows(n, world, rank, C.byref(r0), C.byref(nr)), "shard_rows")
+    return r0.value, nr.value
+
+
+class Backend:
+    """RAII wrapper of a compat-ABI backend handle on one CUDA device
+    (row-sharded over `world` ranks when an NCCL unique id is given)."""
+
+    def __init__(self, dev: int = 0, world: int = 1, rank: int = 0, nccl_id: bytes | None = None):
+        if nccl_id is None:
+            self.h = lib().ggml_backend_xdna_init(dev)
+        else:
+            self.h = lib().ggml_backend_xdna_init_sharded(dev, world, rank, nccl_id)
         if not self.h:
-            raise RuntimeError(f"ggml_backend_xdna_init({dev}) failed: {last_error()}")
-        self.dev = dev
+            raise RuntimeError(f"ggml_backend_xdna_init(dev={dev}, world={world}, rank={rank}) failed: {last_error()}")
+        self.dev, self.world, self.rank = dev, world, rank
 
     def supports_op(self, node: GgmlTensorXdna) -> bool:
         return bool(lib().ggml_backend_xdna_supports_op(self.h, C.byref(node)))
@@ -162,6 +184,10 @@ class Backend:
 
     def synchronize(self) -> None:
         lib().ggml_backend_xdna_synchronize(self.h)
+
+    @property
+    def stream(self) -> int:
+        return lib().ggml_backend_xdna_get_stream(self.h) or 0
 
     def close(self) -> None:
         if self.h:
@@ -199,6 +225,15 @@ class Buffer:
         t.data = self.base + off
         self._next = off + n
         return t
+
+    @staticmethod
+    def copy(src: GgmlTensorXdna, dst: GgmlTensorXdna) -> None:
+        if not lib().ggml_backend_xdna_buffer_cpy_tensor(C.byref(src), C.byref(dst)):
+            raise RuntimeError(f"cpy_tensor failed: {last_error()}")
+
+    def set_device(self, t: GgmlTensorXdna, dev_ptr: int, offset: int, size: int) -> None:
+        if not lib().ggml_backend_xdna_buffer_set_tensor_device(self.h, C.byref(t), dev_ptr, offset, size):
+            raise RuntimeError(f"set_tensor_device failed: {last_error()}")
 
     def set(self, t: GgmlTensorXdna, host_ptr: int, offset: int, size: int) -> None:
         if not lib().ggml_backend_xdna_buffer_set_tensor(self.h, C.byref(t), host_ptr, offset, size):
