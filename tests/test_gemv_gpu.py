@@ -86,6 +86,25 @@ def test_sweep_shapes_config2(cuda, G, O, name, N, K):
     check_parity(y, O.gemv(t, raw, N, K, x), f"{name} {N}x{K}")
 
 
+@pytest.mark.parametrize("name", TYPES)
+@pytest.mark.parametrize("N,K", [(64, 512), (37, 768), (16, 256 * 43), (48, 2048)])
+def test_device_repack_matches_host_layout(cuda, G, name, N, K):
+    # the GPU repack must produce exactly the layout the host reference
+    # implementation of formats.cuh describes, and unpack must invert it
+    t = G.CLAIMED[name]
+    raw = random_blocks(t, N, K, seed=N * K)
+    host = np.zeros_like(raw)
+    G.check(G.lib().b200_repack_host(t, raw.ctypes.data, host.ctypes.data, N, K), "repack_host")
+    d_raw = to_dev(cuda, raw)
+    d_pk = cuda.zeros_like(d_raw)
+    d_back = cuda.zeros_like(d_raw)
+    G.check(G.lib().b200_repack(t, d_raw.data_ptr(), d_pk.data_ptr(), N, K, 0), "repack")
+    G.check(G.lib().b200_unpack(t, d_pk.data_ptr(), d_back.data_ptr(), N, K, 0), "unpack")
+    cuda.cuda.synchronize()
+    assert np.array_equal(d_pk.cpu().numpy(), host)
+    assert np.array_equal(d_back.cpu().numpy(), raw)
+
+
 def test_quantizers_match_oracle(cuda, G, O):
     for t in (G.Q4_0, G.Q4_K):
         N, K = 64, 2048

@@ -20,7 +20,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libggml-b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["gemv.cu", "repack.cu", "quantize.cu"]
+CU_SOURCES = ["gemv.cu", "gemv_mma.cu", "repack.cu", "quantize.cu"]
 CXX_SOURCES = ["backend.cpp"]
 HEADERS = ["formats.cuh", "gemv.cuh", "nccl_shim.h"]
 

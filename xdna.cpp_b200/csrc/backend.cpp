@@ -296,7 +296,35 @@ struct Backend {
         size_t bytes;
     };
     std::vector<PendingOut> pending;
+    // x-digit scratch of the MMA GEMV path: two slots, alternated per launch so
+    // that one GEMV may overlap (PDL) the next launch's x preparation
+    void* xscratch[2] = {nullptr, nullptr};
+    size_t xscratch_bytes = 0;
+    int xscratch_next = 0;
 };
+
+// A scratch slot of at least xprep_bytes(K); growing it drains the stream first.
+void* backend_xscratch(Backend* be, int64_t K);
+
+void* backend_xscratch(Backend* be, int64_t K) {
+    const size_t need = xprep_bytes(K);
+    if (need > be->xscratch_bytes) {
+        if (cudaStreamSynchronize(be->stream) != cudaSuccess) return nullptr;
+        const size_t cap = std::max<size_t>(need, 1u << 20);
+        for (int s = 0; s < 2; ++s) {
+            if (be->xscratch[s]) cudaFree(be->xscratch[s]);
+            be->xscratch[s] = nullptr;
+            if (!cuda_ok(cudaMalloc(&be->xscratch[s], cap), "x scratch alloc")) {
+                be->xscratch_bytes = 0;
+                return nullptr;
+            }
+        }
+        be->xscratch_bytes = cap;
+    }
+    void* p = be->xscratch[be->xscratch_next];
+    be->xscratch_next ^= 1;
+    return p;
+}
 
 Backend* as_backend(void* p) {
     auto* b = static_cast<Backend*>(p);
@@ -325,13 +353,14 @@ std::vector<Chunk> chunks_for(const TensorInfo& ti, size_t off, size_t size, siz
     std::vector<Chunk> out;
     const size_t rb = static_cast<size_t>(ti.mat_bytes / std::max<int64_t>(ti.N, 1));
     if (rb == 0 || size == 0) return out;
-    const int64_t tile_rows_per_chunk =
-        std::max<int64_t>(TILE_ROWS, static_cast<int64_t>(slot_bytes / (rb * TILE_ROWS)) * TILE_ROWS);
+    // 16-row granularity suits both layouts (stripe tiles of 8, MMA tiles of 16 rows)
+    const int64_t tile_rows_per_chunk = std::max<int64_t>(
+        MMA_TILE_ROWS, static_cast<int64_t>(slot_bytes / (rb * MMA_TILE_ROWS)) * MMA_TILE_ROWS);
     const size_t end = off + size;
     for (int64_t m = off / ti.mat_bytes; m < ti.nmat && static_cast<size_t>(m) * ti.mat_bytes < end; ++m) {
         const size_t mb = static_cast<size_t>(m) * ti.mat_bytes;
         const size_t lo = std::max(off, mb) - mb, hi = std::min(end, mb + ti.mat_bytes) - mb;
-        int64_t r0 = static_cast<int64_t>(lo / rb) / TILE_ROWS * TILE_ROWS;
+        int64_t r0 = static_cast<int64_t>(lo / rb) / MMA_TILE_ROWS * MMA_TILE_ROWS;
         const int64_t r1 = static_cast<int64_t>((hi + rb - 1) / rb);
         while (r0 < r1) {
             const int64_t n = std::min<int64_t>(tile_rows_per_chunk, ti.N - r0);
@@ -724,6 +753,10 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
                     if (!yd) return false;
                 }
                 LaunchOpts lo;
+                if (layout_kind(src0->type, N, K) == 1) {
+                    lo.scratch = backend_xscratch(be, K);
+                    if (!lo.scratch) return false;
+                }
                 float* y_local = sharded ? yd + be->rank * N : yd;
                 if (!cuda_ok(gemv_launch(src0->type, w_dev, xd, y_local, N, K, be->stream, lo), "gemv launch"))
                     return false;
@@ -850,6 +883,8 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         be->dev_arena.release();
         be->host_arena.release();
         be->wt_arena.release();
+        for (void* p : be->xscratch)
+            if (p) cudaFree(p);
         if (be->comm) nccl_api().CommDestroy(be->comm);
         cudaStreamDestroy(be->stream);
         be->magic = 0;
@@ -1240,6 +1275,20 @@ static int host_repack(int type, const void* src, void* dst, int64_t n, int64_t 
     if (!f.block_vals || k < 0 || k % f.block_vals || n < 0 || (n > 0 && (!src || !dst))) {
         set_error("b200_%s_host: bad arguments", pack ? "repack" : "unpack");
         return -1;
+    }
+    if (layout_kind(type, n, k) == 1) {
+        const size_t rb = static_cast<size_t>(k / 256) * 144;
+        for (int64_t t = 0; t < n / MMA_TILE_ROWS; ++t)
+            for (int64_t gi = 0; gi < k / 256; ++gi) {
+                const size_t tb = static_cast<size_t>(t) * MMA_TILE_ROWS * rb;
+                if (pack)
+                    mma_pack_group(type, static_cast<const uint8_t*>(src) + tb, rb, gi,
+                                   static_cast<uint8_t*>(dst) + tb + gi * MMA_GROUP_BYTES);
+                else
+                    mma_unpack_group(type, static_cast<const uint8_t*>(src) + tb + gi * MMA_GROUP_BYTES, rb, gi,
+                                     static_cast<uint8_t*>(dst) + tb);
+            }
+        return 0;
     }
     const Geometry g = make_geometry(type, n, k);
     for (int64_t t = 0; t < g.ntiles; ++t) {

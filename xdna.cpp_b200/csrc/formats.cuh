@@ -325,4 +325,114 @@ XB_HD void unrepack_one(const Geometry& g, int tr, int r, int64_t b, const uint8
     unpack_block(f.type, pieces, aux, d, raw + r * g.row_bytes + b * f.block_bytes);
 }
 
+// ---------------------------------------------------------------------------
+// MMA layout (Q4_0 and Q4_K when N % 16 == 0 and K % 256 == 0).
+//
+// The integer tensor-core GEMV (gemv_mma.cu) computes 16 rows x 256 values
+// ("a group": eight 32-value blocks) with mma.m16n8k32: the weights are the
+// u8 A operand, x is three signed-byte digit planes in a block-diagonal B
+// operand whose column n holds block n, so each C column is one block's dot
+// product.  A tile holds 16 rows; a group of a tile is 2304 bytes (16 rows x
+// 144 / 16 rows x 8 blocks x 18), laid out as
+//   A   : [4 chunk pairs][32 lanes][16 B]: lane (g = lane / 4, t = lane % 4)
+//         holds, for chunks c = 2i, 2i + 1, two words: word 0 = block t,
+//         word 1 = block t + 4; byte j of a word = value 4c + j of that block
+//         with row g in the low nibble and row g + 8 in the high nibble
+//         (exactly the m16n8k32 A fragment after one mask / shift);
+//   hdr : 256 B.  Q4_K: the 16 rows' 16-byte headers {d, dmin, scales[12]}.
+//         Q4_0: [g][t][4 x fp16] = d(g, 2t), d(g, 2t+1), d(g+8, 2t), d(g+8, 2t+1)
+//         (the blocks whose C columns lane (g, t) owns).
+// ---------------------------------------------------------------------------
+constexpr int MMA_TILE_ROWS = 16;
+constexpr int MMA_GROUP_BYTES = 2304;
+
+XB_HD int layout_kind(int type, int64_t N, int64_t K) {
+    return ((type == T_Q4_0 || type == T_Q4_K) && N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0) ? 1 : 0;
+}
+
+// 4-bit quant of (row r of a GGUF row pointer, value v of the 256-value group gi)
+XB_HD uint32_t q4_of(int type, const uint8_t* row, int64_t gi, int v) {
+    if (type == T_Q4_K) {
+        const uint8_t* qs = row + gi * 144 + 16;
+        const int j = v >> 5, o = v & 31;
+        return (qs[32 * (j >> 1) + o] >> (4 * (j & 1))) & 0xFu;
+    }
+    const uint8_t* blk = row + (gi * 8 + (v >> 5)) * 18;  // Q4_0
+    const int o = v & 31;
+    return (blk[2 + (o & 15)] >> (4 * (o >> 4))) & 0xFu;
+}
+
+// One group (gi) of one 16-row tile: GGUF rows (tile row 0 at `raw`, stride
+// row_bytes) -> MMA layout at `out` (2304 bytes), or the inverse.
+XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64_t gi, uint8_t* out) {
+    for (int lane = 0; lane < 32; ++lane) {
+        const int g = lane >> 2, t = lane & 3;
+        const uint8_t* r0 = raw + g * row_bytes;
+        const uint8_t* r8 = raw + (g + 8) * row_bytes;
+        for (int c = 0; c < 8; ++c)
+            for (int kind = 0; kind < 2; ++kind) {
+                const int blk = t + 4 * kind;
+                uint32_t w = 0;
+                for (int j = 0; j < 4; ++j) {
+                    const int v = 32 * blk + 4 * c + j;
+                    w |= (q4_of(type, r0, gi, v) | (q4_of(type, r8, gi, v) << 4)) << (8 * j);
+                }
+                put32(out + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * kind, w);
+            }
+    }
+    uint8_t* hdr = out + 2048;
+    if (type == T_Q4_K) {
+        for (int r = 0; r < 16; ++r) copy_bytes(hdr + 16 * r, raw + r * row_bytes + gi * 144, 16);
+    } else {
+        for (int g = 0; g < 8; ++g)
+            for (int t = 0; t < 4; ++t)
+                for (int h = 0; h < 4; ++h) {
+                    const int row = g + 8 * (h >> 1), blk = 2 * t + (h & 1);
+                    copy_bytes(hdr + ((g * 4 + t) * 4 + h) * 2, raw + row * row_bytes + (gi * 8 + blk) * 18, 2);
+                }
+    }
+}
+
+XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
+    const uint8_t* hdr = in + 2048;
+    if (type == T_Q4_K) {
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 144, hdr + 16 * r, 16);
+    } else {
+        for (int g = 0; g < 8; ++g)
+            for (int t = 0; t < 4; ++t)
+                for (int h = 0; h < 4; ++h) {
+                    const int row = g + 8 * (h >> 1), blk = 2 * t + (h & 1);
+                    copy_bytes(raw + row * row_bytes + (gi * 8 + blk) * 18, hdr + ((g * 4 + t) * 4 + h) * 2, 2);
+                }
+    }
+    for (int lane = 0; lane < 32; ++lane) {
+        const int g = lane >> 2, t = lane & 3;
+        for (int c = 0; c < 8; ++c)
+            for (int kind = 0; kind < 2; ++kind) {
+                const int blk = t + 4 * kind;
+                const uint32_t w = get32(in + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * kind);
+                for (int j = 0; j < 4; ++j) {
+                    const int v = 32 * blk + 4 * c + j;
+                    const uint32_t b = (w >> (8 * j)) & 0xFFu;
+                    for (int half = 0; half < 2; ++half) {
+                        uint8_t* row = raw + (g + 8 * half) * row_bytes;
+                        const uint32_t q = (b >> (4 * half)) & 0xFu;
+                        uint8_t* p;
+                        int sh;
+                        if (type == T_Q4_K) {
+                            const int jj = v >> 5, o = v & 31;
+                            p = row + gi * 144 + 16 + 32 * (jj >> 1) + o;
+                            sh = 4 * (jj & 1);
+                        } else {
+                            const int o = v & 31;
+                            p = row + (gi * 8 + (v >> 5)) * 18 + 2 + (o & 15);
+                            sh = 4 * (o >> 4);
+                        }
+                        *p = uint8_t((*p & ~(0xFu << sh)) | (q << sh));
+                    }
+                }
+            }
+    }
+}
+
 }  // namespace xb

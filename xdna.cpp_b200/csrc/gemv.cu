@@ -755,6 +755,11 @@ cudaError_t launch_typed(const uint8_t* W, const float* x, float* y, int64_t N, 
 cudaError_t gemv_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
                         cudaStream_t stream, const LaunchOpts& opts) {
     if (N == 0) return cudaSuccess;
+    if (layout_kind(type, N, K) == 1) {
+        void* scratch = opts.scratch ? opts.scratch : launcher_scratch(stream, K);
+        if (!scratch) return cudaErrorMemoryAllocation;
+        return gemv_mma_launch(type, W, x, y, N, K, scratch, stream, opts.pdl);
+    }
     const uint8_t* w = static_cast<const uint8_t*>(W);
     switch (type) {
         case T_Q4_0: return launch_typed<DecQ4_0>(w, x, y, N, K, stream, opts);

@@ -40,7 +40,8 @@ cudaError_t check_args(int type, int64_t N, int64_t K, int64_t row0, int64_t nro
     const FormatInfo f = format_info(type);
     if (!f.block_vals || K < 0 || K % f.block_vals || N < 0 || row0 < 0 || nrows < 0 || row0 + nrows > N)
         return cudaErrorInvalidValue;
-    if (row0 % TILE_ROWS || (nrows % TILE_ROWS && row0 + nrows != N)) return cudaErrorInvalidValue;
+    const int tr = layout_kind(type, N, K) == 1 ? MMA_TILE_ROWS : TILE_ROWS;
+    if (row0 % tr || (nrows % tr && row0 + nrows != N)) return cudaErrorInvalidValue;
     return cudaSuccess;
 }
 
@@ -50,6 +51,7 @@ cudaError_t repack_launch(int type, const void* raw, void* packed, int64_t N, in
                           int64_t nrows, cudaStream_t stream) {
     cudaError_t e = check_args(type, N, K, row0, nrows);
     if (e != cudaSuccess || nrows == 0 || K == 0) return e;
+    if (layout_kind(type, N, K) == 1) return mma_repack_launch(type, raw, packed, nrows, K, true, stream);
     const int64_t total = nrows * (K / format_info(type).block_vals);
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads < 65536 ? (total + threads - 1) / threads : 65536;
@@ -62,6 +64,7 @@ cudaError_t unpack_launch(int type, const void* packed, void* raw, int64_t N, in
                           int64_t nrows, cudaStream_t stream) {
     cudaError_t e = check_args(type, N, K, row0, nrows);
     if (e != cudaSuccess || nrows == 0 || K == 0) return e;
+    if (layout_kind(type, N, K) == 1) return mma_repack_launch(type, packed, raw, nrows, K, false, stream);
     const int64_t total = nrows * (K / format_info(type).block_vals);
     const int threads = 256;
     const int64_t blocks = (total + threads - 1) / threads < 65536 ? (total + threads - 1) / threads : 65536;
