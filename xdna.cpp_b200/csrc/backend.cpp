@@ -303,18 +303,19 @@ struct Backend {
     int xscratch_next = 0;
 };
 
-// A scratch slot of at least xprep_bytes(K); growing it drains the stream first.
-void* backend_xscratch(Backend* be, int64_t K);
+// A scratch slot of at least xprep_bytes(N, K); growing it drains the stream first.
+void* backend_xscratch(Backend* be, int64_t N, int64_t K);
 
-void* backend_xscratch(Backend* be, int64_t K) {
-    const size_t need = xprep_bytes(K);
+void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
+    const size_t need = xprep_bytes(N, K);
     if (need > be->xscratch_bytes) {
         if (cudaStreamSynchronize(be->stream) != cudaSuccess) return nullptr;
         const size_t cap = std::max<size_t>(need, 1u << 20);
         for (int s = 0; s < 2; ++s) {
             if (be->xscratch[s]) cudaFree(be->xscratch[s]);
             be->xscratch[s] = nullptr;
-            if (!cuda_ok(cudaMalloc(&be->xscratch[s], cap), "x scratch alloc")) {
+            if (!cuda_ok(cudaMalloc(&be->xscratch[s], cap), "x scratch alloc") ||
+                !cuda_ok(cudaMemset(be->xscratch[s], 0, cap), "x scratch clear")) {
                 be->xscratch_bytes = 0;
                 return nullptr;
             }
@@ -754,7 +755,7 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
                 }
                 LaunchOpts lo;
                 if (layout_kind(src0->type, N, K) == 1) {
-                    lo.scratch = backend_xscratch(be, K);
+                    lo.scratch = backend_xscratch(be, N, K);
                     if (!lo.scratch) return false;
                 }
                 float* y_local = sharded ? yd + be->rank * N : yd;

@@ -756,7 +756,7 @@ cudaError_t gemv_launch(int type, const void* W, const float* x, float* y, int64
                         cudaStream_t stream, const LaunchOpts& opts) {
     if (N == 0) return cudaSuccess;
     if (layout_kind(type, N, K) == 1) {
-        void* scratch = opts.scratch ? opts.scratch : launcher_scratch(stream, K);
+        void* scratch = opts.scratch ? opts.scratch : launcher_scratch(stream, N, K);
         if (!scratch) return cudaErrorMemoryAllocation;
         return gemv_mma_launch(type, W, x, y, N, K, scratch, stream, opts.pdl);
     }

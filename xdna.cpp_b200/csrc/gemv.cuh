@@ -8,14 +8,18 @@ namespace xb {
 
 struct LaunchOpts {
     bool pdl = false;          // programmatic dependent launch (overlap with the previous kernel)
-    void* scratch = nullptr;   // x-digit scratch of xprep_bytes(K) for the MMA path (nullptr: internal)
+    void* scratch = nullptr;   // MMA-path scratch of xprep_bytes(N, K), zeroed when new (nullptr: internal)
 };
 
 // MMA path (gemv_mma.cu): scratch bytes for one x vector of length K, the
 // launcher's internal per-(device, stream) scratch, the two kernels and the
 // MMA-layout repack of whole 16-row tiles (raw / packed point at the first row).
-size_t xprep_bytes(int64_t K);
-void* launcher_scratch(cudaStream_t stream, int64_t K);
+struct ScratchLayout {
+    size_t frags, scale, xsum, queue, total;
+};
+ScratchLayout scratch_layout(int64_t N, int64_t K);
+size_t xprep_bytes(int64_t N, int64_t K);
+void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K);
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K, void* scratch,
                             cudaStream_t stream, bool pdl);
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,

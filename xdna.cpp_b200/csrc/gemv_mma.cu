@@ -36,19 +36,10 @@
 namespace xb {
 namespace {
 
-constexpr int kMmaThreads = 256;
-constexpr int kMmaWarps = kMmaThreads / 32;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-__device__ __forceinline__ uint4 ld_stream(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
 __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
     return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
@@ -70,10 +61,12 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //   holding the digits of values 4*chunk .. 4*chunk + 3 (byte j = value 4c+j);
 //   scale[b] = 2^e_b; xsum[b] = sum of the block's x (F32).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ frags,
-                                                    float* __restrict__ scale, float* __restrict__ xsum) {
+__global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ frags,
+                                                    float* __restrict__ scale, float* __restrict__ xsum,
+                                                    int* __restrict__ queue) {
     pdl_release();
     pdl_wait();
+    if (blockIdx.x == 0 && threadIdx.x == 0) *queue = 0;  // tile queue of the GEMV that follows
     const int lane = threadIdx.x & 31;
     const int64_t nblk = K / 32;
     for (int64_t b = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; b < nblk;
@@ -109,95 +102,144 @@ __global__ void __launch_bounds__(256) xprep_kernel(const float* __restrict__ x,
 }
 
 // ---------------------------------------------------------------------------
-// GEMV: one CTA per 16-row tile at a time, its warps split the groups (K)
-// and combine through shared memory.
+// GEMV.  A CTA of 8 warps works on one 16-row tile at a time; warp w takes
+// groups w, w + 8, ... of the tile and the warps combine their partial rows
+// through shared memory.  Tiles come from a queue (first one static, then an
+// atomic counter that xprep_kernel zeroes), so CTAs that finish early take
+// more work instead of idling at the tail.  Each warp keeps DRAM busy ahead
+// of its loads with one bulk L2 prefetch per group (cp.async.bulk.prefetch:
+// no registers, no completion to track) for the groups it will read next.
 // ---------------------------------------------------------------------------
-template <int TYPE>
-__global__ void __launch_bounds__(kMmaThreads, 3)
-    gemv_mma_kernel(const uint8_t* __restrict__ W, const uint4* __restrict__ frags, const float* __restrict__ scale,
-                    const float* __restrict__ xsum, float* __restrict__ y, int64_t N, int64_t K) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t ngroups = K / 256, ntiles = N / MMA_TILE_ROWS;
-    const int64_t tile_bytes = ngroups * MMA_GROUP_BYTES;
-    const bool bsrc = (g & 3) == t;  // this lane supplies a B (x digit) fragment
-    __shared__ float red[kMmaWarps][MMA_TILE_ROWS];
-    pdl_release();
-    bool waited = false;
+constexpr int kWarps = 8;
+constexpr int kGemvThreads = kWarps * 32;
+constexpr int kPrefetch = 3;  // groups ahead per warp
 
-    for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const uint8_t* tbase = W + tile * tile_bytes;
+struct GemvArgs {
+    const uint8_t* W;
+    const uint4* frags;   // x digits, 64 x 16 B per group
+    const float* scale;   // per 32-value block
+    const float* xsum;
+    float* y;
+    int* queue;           // tile counter, zeroed by xprep
+    int64_t N, K;
+    int64_t ntiles, ngroups;
+};
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
+// bA / bB are this lane's B registers; only their owning lanes ever load them,
+// so elsewhere they stay zero without being cleared per chunk.
+template <int TYPE>
+__device__ __forceinline__ void group_dot(const uint8_t* gb, const uint4* __restrict__ fg, const float* __restrict__ sc_,
+                                          const float* __restrict__ xs_, int lane, int g, int t, bool ldA, bool ldB,
+                                          uint4& bA, uint4& bB, float& y0, float& y8) {
+    uint4 A[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
+    uint4 h0, h8;
+    uint2 d4;
+    if (TYPE == T_Q4_K) {
+        h0 = ld_stream(gb + 2048 + 16 * g);
+        h8 = ld_stream(gb + 2048 + 16 * (g + 8));
+    } else {
+        d4 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + lane);
+    }
+    int C[3][4];
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) C[p][k] = 0;
+    // x digits of all eight chunks first (independent registers, so the
+    // loads overlap); only the 8 owning lanes load, the rest keep zeros
+    fg += g;
+    uint4 bf[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) bf[c] = (ldA || ldB) ? __ldg(fg + c * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
+        const uint32_t a0 = w0 & 0x0F0F0F0Fu, a1 = (w0 >> 4) & 0x0F0F0F0Fu;
+        const uint32_t a2 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
+        mma_u8s8(C[0], a0, a1, a2, a3, ldA ? bf[c].x : 0u, ldB ? bf[c].x : 0u);
+        mma_u8s8(C[1], a0, a1, a2, a3, ldA ? bf[c].y : 0u, ldB ? bf[c].y : 0u);
+        mma_u8s8(C[2], a0, a1, a2, a3, ldA ? bf[c].z : 0u, ldB ? bf[c].z : 0u);
+    }
+    // C[p][0]: (row g, block 2t)  [1]: (g, 2t+1)  [2]: (g+8, 2t)  [3]: (g+8, 2t+1).
+    // |D2| <= 64, so the combined integer fits int32: 32 * 15 * (64 * 65536 + 128 * 257) < 2^31.
+    float T[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) T[k] = static_cast<float>(C[2][k] * 65536 + C[1][k] * 256 + C[0][k]);
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
+    const float2 xs2 = __ldg(reinterpret_cast<const float2*>(xs_) + t);
+    const float s0 = sc2.x, s1 = sc2.y, x0 = xs2.x, x1 = xs2.y;
+    if (TYPE == T_Q4_K) {
+        // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four per word
+        const int sh = 16 * (t & 1);
+        float sc[2][2], mn[2][2], d[2], dm[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint4 hh = h ? h8 : h0;
+            const uint32_t scw = t < 2 ? (hh.y & 0x3F3F3F3Fu) : ((hh.w & 0x0F0F0F0Fu) | ((hh.y >> 2) & 0x30303030u));
+            const uint32_t mw = t < 2 ? (hh.z & 0x3F3F3F3Fu)
+                                      : (((hh.w >> 4) & 0x0F0F0F0Fu) | ((hh.z >> 2) & 0x30303030u));
+            sc[h][0] = static_cast<float>((scw >> sh) & 0xFFu);
+            sc[h][1] = static_cast<float>((scw >> (sh + 8)) & 0xFFu);
+            mn[h][0] = static_cast<float>((mw >> sh) & 0xFFu);
+            mn[h][1] = static_cast<float>((mw >> (sh + 8)) & 0xFFu);
+            d[h] = h2f(hh.x);
+            dm[h] = h2f(hh.x >> 16);
+        }
+        y0 = fmaf(d[0], fmaf(sc[0][0] * s0, T[0], sc[0][1] * s1 * T[1]),
+                  fmaf(-dm[0], fmaf(mn[0][0], x0, mn[0][1] * x1), y0));
+        y8 = fmaf(d[1], fmaf(sc[1][0] * s0, T[2], sc[1][1] * s1 * T[3]),
+                  fmaf(-dm[1], fmaf(mn[1][0], x0, mn[1][1] * x1), y8));
+    } else {
+        // value = (q - 8) * d; d of (g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+        const float dg0 = h2f(d4.x), dg1 = h2f(d4.x >> 16), d80 = h2f(d4.y), d81 = h2f(d4.y >> 16);
+        y0 = fmaf(dg0, fmaf(s0, T[0], -8.0f * x0), fmaf(dg1, fmaf(s1, T[1], -8.0f * x1), y0));
+        y8 = fmaf(d80, fmaf(s0, T[2], -8.0f * x0), fmaf(d81, fmaf(s1, T[3], -8.0f * x1), y8));
+    }
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(kGemvThreads, 3) gemv_mma_kernel(const GemvArgs a) {
+    __shared__ float red[kWarps][MMA_TILE_ROWS];
+    __shared__ int64_t next_tile;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int64_t tile_bytes = a.ngroups * MMA_GROUP_BYTES;
+    const bool bsrc = (g & 3) == t;  // this lane supplies a B (x digit) fragment
+    const bool ldA = bsrc && g < 4, ldB = bsrc && g >= 4;
+    uint4 bA = make_uint4(0, 0, 0, 0), bB = make_uint4(0, 0, 0, 0);
+
+    // the first tile is static: start its weights towards L2 before waiting on xprep
+    int64_t tile = blockIdx.x;
+    if (lane == 0 && tile < a.ntiles)
+        for (int d = 0; d < kPrefetch; ++d) {
+            const int64_t gi = warp + int64_t(d) * kWarps;
+            if (gi < a.ngroups) prefetch_l2(a.W + tile * tile_bytes + gi * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+        }
+    pdl_release();
+    pdl_wait();  // x digits and the tile queue come from xprep_kernel
+
+    while (tile < a.ntiles) {  // `tile` is CTA-uniform, so every thread runs the same iterations
+        if (threadIdx.x == 0) next_tile = static_cast<int64_t>(gridDim.x) + atomicAdd(a.queue, 1);
+        const uint8_t* tb = a.W + tile * tile_bytes;
         float y0 = 0.f, y8 = 0.f;
-        for (int64_t gi = warp; gi < ngroups; gi += kMmaWarps) {
-            const uint8_t* gb = tbase + gi * MMA_GROUP_BYTES;
-            uint4 A[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
-            uint4 h0, h8;
-            uint2 d4;
-            if (TYPE == T_Q4_K) {
-                h0 = ld_stream(gb + 2048 + 16 * g);
-                h8 = ld_stream(gb + 2048 + 16 * (g + 8));
-            } else {
-                d4 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + lane);
-            }
-            if (!waited) {
-                pdl_wait();  // x digits are produced by the previous kernel
-                waited = true;
-            }
-            int C[3][4];
-#pragma unroll
-            for (int p = 0; p < 3; ++p)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) C[p][k] = 0;
-            const uint4* fg = frags + gi * 64;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
-                const uint32_t a0 = w0 & 0x0F0F0F0Fu, a1 = (w0 >> 4) & 0x0F0F0F0Fu;
-                const uint32_t a2 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-                const uint4 bf = bsrc ? __ldg(fg + c * 8 + g) : make_uint4(0, 0, 0, 0);
-                const bool lo = g < 4;
-                mma_u8s8(C[0], a0, a1, a2, a3, lo ? bf.x : 0u, lo ? 0u : bf.x);
-                mma_u8s8(C[1], a0, a1, a2, a3, lo ? bf.y : 0u, lo ? 0u : bf.y);
-                mma_u8s8(C[2], a0, a1, a2, a3, lo ? bf.z : 0u, lo ? 0u : bf.z);
-            }
-            // C[p][0]: (row g, block 2t)  [1]: (g, 2t+1)  [2]: (g+8, 2t)  [3]: (g+8, 2t+1)
-            float T[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f,
-                            fmaf(static_cast<float>(C[1][k]), 256.0f, static_cast<float>(C[0][k])));
-            const int64_t b0 = gi * 8 + 2 * t;
-            const float s0 = __ldg(scale + b0), s1 = __ldg(scale + b0 + 1);
-            const float x0 = __ldg(xsum + b0), x1 = __ldg(xsum + b0 + 1);
-            if (TYPE == T_Q4_K) {
-                // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four at a time
-                const int sh = 16 * (t & 1);
-                float sc[2][2], mn[2][2], d[2], dm[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint4 hh = h ? h8 : h0;
-                    const uint32_t scw = t < 2 ? (hh.y & 0x3F3F3F3Fu)
-                                               : ((hh.w & 0x0F0F0F0Fu) | ((hh.y >> 2) & 0x30303030u));
-                    const uint32_t mw = t < 2 ? (hh.z & 0x3F3F3F3Fu)
-                                              : (((hh.w >> 4) & 0x0F0F0F0Fu) | ((hh.z >> 2) & 0x30303030u));
-                    sc[h][0] = static_cast<float>((scw >> sh) & 0xFFu);
-                    sc[h][1] = static_cast<float>((scw >> (sh + 8)) & 0xFFu);
-                    mn[h][0] = static_cast<float>((mw >> sh) & 0xFFu);
-                    mn[h][1] = static_cast<float>((mw >> (sh + 8)) & 0xFFu);
-                    d[h] = h2f(hh.x);
-                    dm[h] = h2f(hh.x >> 16);
-                }
-                y0 = fmaf(d[0], fmaf(sc[0][0] * s0, T[0], sc[0][1] * s1 * T[1]),
-                          fmaf(-dm[0], fmaf(mn[0][0], x0, mn[0][1] * x1), y0));
-                y8 = fmaf(d[1], fmaf(sc[1][0] * s0, T[2], sc[1][1] * s1 * T[3]),
-                          fmaf(-dm[1], fmaf(mn[1][0], x0, mn[1][1] * x1), y8));
-            } else {
-                // d(g, 2t), d(g, 2t+1), d(g+8, 2t), d(g+8, 2t+1); value = (q - 8) * d
-                const float dg0 = h2f(d4.x), dg1 = h2f(d4.x >> 16), d80 = h2f(d4.y), d81 = h2f(d4.y >> 16);
-                y0 = fmaf(dg0, fmaf(s0, T[0], -8.0f * x0), fmaf(dg1, fmaf(s1, T[1], -8.0f * x1), y0));
-                y8 = fmaf(d80, fmaf(s0, T[2], -8.0f * x0), fmaf(d81, fmaf(s1, T[3], -8.0f * x1), y8));
-            }
+        for (int64_t gi = warp; gi < a.ngroups; gi += kWarps) {
+            const int64_t ahead = gi + int64_t(kPrefetch) * kWarps;
+            if (lane == 0 && ahead < a.ngroups) prefetch_l2(tb + ahead * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+            group_dot<TYPE>(tb + gi * MMA_GROUP_BYTES, a.frags + gi * 64, a.scale + gi * 8, a.xsum + gi * 8, lane, g,
+                            t, ldA, ldB, bA, bB, y0, y8);
         }
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
@@ -208,15 +250,22 @@ __global__ void __launch_bounds__(kMmaThreads, 3)
             red[warp][g + 8] = y8;
         }
         __syncthreads();
+        const int64_t nt = next_tile;
         if (threadIdx.x < MMA_TILE_ROWS) {
-            float a = 0.f;
-            const int nw = static_cast<int>(ngroups < kMmaWarps ? ngroups : kMmaWarps);
-            for (int w = 0; w < nw; ++w) a += red[w][threadIdx.x];
-            y[tile * MMA_TILE_ROWS + threadIdx.x] = a;
+            float acc = 0.f;
+            const int nw = static_cast<int>(a.ngroups < kWarps ? a.ngroups : kWarps);
+            for (int w = 0; w < nw; ++w) acc += red[w][threadIdx.x];
+            a.y[tile * MMA_TILE_ROWS + threadIdx.x] = acc;
         }
+        // warm L2 with the next tile's first groups of this warp
+        if (lane == 0 && nt < a.ntiles)
+            for (int d = 0; d < kPrefetch; ++d) {
+                const int64_t gi = warp + int64_t(d) * kWarps;
+                if (gi < a.ngroups) prefetch_l2(a.W + nt * tile_bytes + gi * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+            }
         __syncthreads();
+        tile = nt;
     }
-    if (!waited) pdl_wait();
 }
 
 // ---------------------------------------------------------------------------
@@ -325,12 +374,23 @@ int g_scratch_n = 0;
 
 }  // namespace
 
-size_t xprep_bytes(int64_t K) {
-    // frags 1024 B per 256 values + scale and xsum per 32 values, 256-aligned pieces
-    const size_t f = static_cast<size_t>(K / 256) * 1024;
-    const size_t m = (static_cast<size_t>(K / 32) * sizeof(float) + 255) & ~size_t(255);
-    return f + 2 * m;
+// Scratch of one MMA GEMV launch: x digits (1 KiB per 256 values), block
+// scales and sums (per 32 values) and the tile queue counter, which
+// xprep_kernel zeroes at the start of every launch.
+ScratchLayout scratch_layout(int64_t N, int64_t K) {
+    (void)N;
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    ScratchLayout L;
+    const int64_t ngroups = K / 256;
+    L.frags = 0;
+    L.scale = up(L.frags + static_cast<size_t>(ngroups) * 1024);
+    L.xsum = up(L.scale + static_cast<size_t>(K / 32) * sizeof(float));
+    L.queue = up(L.xsum + static_cast<size_t>(K / 32) * sizeof(float));
+    L.total = up(L.queue + sizeof(int));
+    return L;
 }
+
+size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,
                               cudaStream_t stream) {
@@ -348,46 +408,53 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
 
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
                             void* scratch, cudaStream_t stream, bool pdl) {
-    uint8_t* frags = static_cast<uint8_t*>(scratch);
-    const size_t m = (static_cast<size_t>(K / 32) * sizeof(float) + 255) & ~size_t(255);
-    float* scale = reinterpret_cast<float*>(frags + static_cast<size_t>(K / 256) * 1024);
-    float* xsum = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scale) + m);
+    const ScratchLayout L = scratch_layout(N, K);
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    GemvArgs a;
+    a.W = static_cast<const uint8_t*>(W);
+    a.frags = reinterpret_cast<const uint4*>(base + L.frags);
+    a.scale = reinterpret_cast<const float*>(base + L.scale);
+    a.xsum = reinterpret_cast<const float*>(base + L.xsum);
+    a.y = y;
+    a.queue = reinterpret_cast<int*>(base + L.queue);
+    a.N = N;
+    a.K = K;
+    a.ntiles = N / MMA_TILE_ROWS;
+    a.ngroups = K / 256;
 
     static int s_sms[16] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 16 && s_sms[dev] == 0) cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int sms = (dev >= 0 && dev < 16 && s_sms[dev] > 0) ? s_sms[dev] : 148;
+    if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
+    if (s_sms[dev] == 0) cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int sms = s_sms[dev] > 0 ? s_sms[dev] : 148;
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-
     cudaLaunchConfig_t cp = {};
     const int64_t nblk = K / 32;
-    cp.gridDim = dim3(static_cast<unsigned>((nblk + 7) / 8));
-    cp.blockDim = dim3(256);
+    cp.gridDim = dim3(static_cast<unsigned>((nblk + 1) / 2));  // one warp per 32-value block
+    cp.blockDim = dim3(64);
     cp.stream = stream;
     cp.attrs = attr;
     cp.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, frags, scale, xsum);
+    cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, base + L.frags, reinterpret_cast<float*>(base + L.scale),
+                                       reinterpret_cast<float*>(base + L.xsum), a.queue);
     if (e != cudaSuccess) return e;
 
-    const int64_t ntiles = N / MMA_TILE_ROWS;
-    int64_t blocks = ntiles < int64_t(sms) * 3 ? ntiles : int64_t(sms) * 3;
+    int64_t blocks = a.ntiles < int64_t(sms) * 3 ? a.ntiles : int64_t(sms) * 3;
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks));
-    cg.blockDim = dim3(kMmaThreads);
+    cg.blockDim = dim3(kGemvThreads);
     cg.stream = stream;
     cudaLaunchAttribute attr2[1];
     attr2[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr2[0].val.programmaticStreamSerializationAllowed = 1;  // overlap the weight prefetch with xprep
+    attr2[0].val.programmaticStreamSerializationAllowed = 1;  // overlap the L2 warm-up with xprep
     cg.attrs = attr2;
     cg.numAttrs = 1;
-    const uint4* fr = reinterpret_cast<const uint4*>(frags);
-    const uint8_t* w = static_cast<const uint8_t*>(W);
-    if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, w, fr, scale, xsum, y, N, K);
-    if (type == T_Q4_0) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, w, fr, scale, xsum, y, N, K);
+    if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
+    if (type == T_Q4_0) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
     return cudaErrorInvalidValue;
 }
 
@@ -395,8 +462,8 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 // alternated so that a GEMV reading one slot can overlap (PDL) the next call's
 // x preparation writing the other.  Grown on demand (must not happen inside
 // stream capture: the first call for a new, larger K allocates).
-void* launcher_scratch(cudaStream_t stream, int64_t K) {
-    const size_t need = xprep_bytes(K);
+void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K) {
+    const size_t need = xprep_bytes(N, K);
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(g_scratch_mtx);
@@ -413,7 +480,7 @@ void* launcher_scratch(cudaStream_t stream, int64_t K) {
         for (int s = 0; s < 2; ++s) {
             if (e->ptr[s]) cudaFree(e->ptr[s]);
             e->ptr[s] = nullptr;
-            if (cudaMalloc(&e->ptr[s], cap) != cudaSuccess) {
+            if (cudaMalloc(&e->ptr[s], cap) != cudaSuccess || cudaMemset(e->ptr[s], 0, cap) != cudaSuccess) {
                 e->bytes = 0;
                 return nullptr;
             }
