@@ -298,3 +298,26 @@ def test_concurrent_threads_share_a_backend(cuda, G, O):
         [x.start() for x in th]
         [x.join() for x in th]
     assert not errors, errors[:4]
+
+
+def test_mma_split_shapes_interleaved_and_deterministic(cuda, G, O):
+    """The 4-bit MMA path splits K into slices and tiles across warps, with
+    per-tile arrival counters that every launch must leave at zero: shapes
+    that share one stream's scratch, interleaved, give the oracle's result
+    each time and identical bits on repeats (fixed summation order)."""
+    cases = [(G.Q4_K, 2048, 256 * 43), (G.Q4_0, 1024, 5120), (G.Q4_K, 64, 512), (G.Q4_K, 4096, 256 * 42),
+             (G.Q4_0, 16, 256), (G.Q4_K, 16384, 2048)]
+    data = []
+    for i, (t, N, K) in enumerate(cases):
+        raw = O.quantize(t, normal_weights(N, K, seed=900 + i))
+        x = normal_x(K, seed=950 + i)
+        data.append((t, N, K, raw, x, O.gemv(t, raw, N, K, x)))
+    first = {}
+    for rep in range(2):
+        for i, (t, N, K, raw, x, ref) in enumerate(data):
+            y = gemv_gpu(cuda, G, t, raw, N, K, x)
+            check_parity(y, ref, f"{G.TYPE_NAME[t]} {N}x{K} rep {rep}")
+            if rep == 0:
+                first[i] = y
+            else:
+                np.testing.assert_array_equal(y, first[i])

@@ -15,7 +15,7 @@ struct LaunchOpts {
 // launcher's internal per-(device, stream) scratch, the two kernels and the
 // MMA-layout repack of whole 16-row tiles (raw / packed point at the first row).
 struct ScratchLayout {
-    size_t frags, scale, xsum, queue, total;
+    size_t frags, zeros, scale, xsum, count, partial, total;
 };
 ScratchLayout scratch_layout(int64_t N, int64_t K);
 size_t xprep_bytes(int64_t N, int64_t K);

@@ -18,8 +18,10 @@
 //     per-block scales (Q4_0 d, Q4_K d * sc and dmin * m) are applied with no
 //     idle lanes.
 //   * weights arrive pre-swizzled (formats.cuh, MMA layout) so one 16-byte
-//     streaming load per lane yields two chunks' A fragments after a mask and
-//     a shift; there is no x reuse problem because B comes from L1/L2.
+//     streaming load per lane yields two chunks' A fragments with one mask
+//     per register (rows g+8 are used in place as 16 q and scaled back in the
+//     integer combine); the x digits (B) come from L1, written once per launch
+//     by xprep_kernel in a per-lane slot layout that needs no selects.
 //
 // Accumulation: exact int32 inside a block, F32 across blocks (the products
 // never round, so the result is at least as accurate as the reference's
@@ -56,21 +58,60 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 }
 
 // ---------------------------------------------------------------------------
-// x preparation: one warp per 32-value block.
-//   frags[(group * 8 + chunk) * 8 + block_in_group] = {D0, D1, D2, 0} words
-//   holding the digits of values 4*chunk .. 4*chunk + 3 (byte j = value 4c+j);
-//   scale[b] = 2^e_b; xsum[b] = sum of the block's x (F32).
+// Work split and scratch.
+//
+// The GEMV's unit of work is one (16-row tile, 256-value group) pair, 2304
+// contiguous bytes of the MMA layout; units are numbered tile-major, so unit u
+// lives at W + u * 2304.  Each warp of the grid takes one contiguous,
+// equal-sized range of units (warp w: [w U / NW, (w + 1) U / NW)), so every
+// warp streams the same number of bytes whatever N and K are: no partial
+// waves, no idle SMs on short matrices.  A tile whose groups are split across
+// warps is finished by the warp that arrives last at the tile's counter: it
+// adds the contributors' partial rows in warp order (deterministic) and
+// writes y.  A warp has at most two split tiles (its first and its last), so
+// its partials need two 16-float slots.
+//
+// Scratch of one launch (all offsets 256-byte aligned):
+//   frags   per group, per chunk c (32 values of each of the 8 blocks), per
+//           block b: a 32-byte B-fragment slot {b0,b1} x 3 digit planes.
+//           Block b < 4 is supplied by lane (g = b, t = b) in register b0,
+//           block b >= 4 by lane (g = b, t = b - 4) in register b1; the other
+//           register of the pair is zero, so the kernel needs no selects.
+//   zeros   32 zero bytes: the B "slot" of the 24 lanes that supply nothing
+//   scale   2^e per 32-value block;  xsum  sum of the block's x
+//   count   one arrival counter per tile (zeroed by xprep_kernel)
+//   partial kMaxCtas * 8 warps * 2 slots * 16 floats
 // ---------------------------------------------------------------------------
+constexpr int kWarps = 8;
+constexpr int kGemvThreads = kWarps * 32;
+constexpr int kCtasPerSm = 3;
+constexpr int kMaxCtas = 512;        // bounds the partial-slot area
+constexpr int kPrefetch = 4;         // groups ahead per warp (bulk L2 prefetch)
+constexpr int kSlotBytes = 32;
+constexpr int kChunkFragBytes = 8 * kSlotBytes;       // 8 blocks
+constexpr int kGroupFragBytes = 8 * kChunkFragBytes;  // 8 chunks: 2 KiB per 256 values
+
+__device__ __forceinline__ uint32_t digit_word(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, int plane) {
+    // byte `plane` of each of four lanes' packed digits, in value order
+    const uint32_t sel = 0x0040u | (static_cast<uint32_t>(plane) * 0x0011u);
+    return __byte_perm(__byte_perm(v0, v1, sel), __byte_perm(v2, v3, sel), 0x5410);
+}
+
+// x preparation: one warp per 32-value block (lane j = value j); also zeroes
+// the tile counters of the GEMV that follows.
 __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ frags,
-                                                    float* __restrict__ scale, float* __restrict__ xsum,
-                                                    int* __restrict__ queue) {
+                                                    uint8_t* __restrict__ zeros, float* __restrict__ scale,
+                                                    float* __restrict__ xsum, int* __restrict__ count,
+                                                    int64_t ntiles) {
     pdl_release();
     pdl_wait();
-    if (blockIdx.x == 0 && threadIdx.x == 0) *queue = 0;  // tile queue of the GEMV that follows
+    const int64_t gtid = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+    const int64_t nthr = int64_t(gridDim.x) * blockDim.x;
+    for (int64_t i = gtid; i < ntiles; i += nthr) count[i] = 0;
+    if (gtid < kSlotBytes / 4) reinterpret_cast<uint32_t*>(zeros)[gtid] = 0u;
     const int lane = threadIdx.x & 31;
     const int64_t nblk = K / 32;
-    for (int64_t b = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; b < nblk;
-         b += (int64_t(gridDim.x) * blockDim.x) >> 5) {
+    for (int64_t b = gtid >> 5; b < nblk; b += nthr >> 5) {
         const float v = x[b * 32 + lane];
         float m = fabsf(v), s = v;
 #pragma unroll
@@ -86,14 +127,27 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
         const int d0 = ((X + 128) & 255) - 128;
         const int X1 = (X - d0) >> 8;
         const int d1 = ((X1 + 128) & 255) - 128;
-        const int d2 = (X1 - d1) >> 8;
-        const int64_t gi = b >> 3;
-        const int blk = static_cast<int>(b & 7), c = lane >> 2, j = lane & 3;
-        uint8_t* w = frags + ((gi * 8 + c) * 8 + blk) * 16;
-        w[j] = static_cast<uint8_t>(d0);
-        w[4 + j] = static_cast<uint8_t>(d1);
-        w[8 + j] = static_cast<uint8_t>(d2);
-        w[12 + j] = 0;
+        const int d2 = (X1 - d1) >> 8;                        // |d2| <= 64
+        const uint32_t mine = (static_cast<uint32_t>(d0) & 0xFFu) | ((static_cast<uint32_t>(d1) & 0xFFu) << 8) |
+                              ((static_cast<uint32_t>(d2) & 0xFFu) << 16);
+        const uint32_t n1 = __shfl_down_sync(0xffffffffu, mine, 1);
+        const uint32_t n2 = __shfl_down_sync(0xffffffffu, mine, 2);
+        const uint32_t n3 = __shfl_down_sync(0xffffffffu, mine, 3);
+        if ((lane & 3) == 0) {  // values 4c .. 4c + 3 of chunk c = lane / 4
+            const uint32_t D0 = digit_word(mine, n1, n2, n3, 0);
+            const uint32_t D1 = digit_word(mine, n1, n2, n3, 1);
+            const uint32_t D2 = digit_word(mine, n1, n2, n3, 2);
+            const int64_t gi = b >> 3;
+            const int blk = static_cast<int>(b & 7), c = lane >> 2;
+            uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
+            if (blk < 4) {
+                slot[0] = make_uint4(D0, 0u, D1, 0u);
+                slot[1] = make_uint4(D2, 0u, 0u, 0u);
+            } else {
+                slot[0] = make_uint4(0u, D0, 0u, D1);
+                slot[1] = make_uint4(0u, D2, 0u, 0u);
+            }
+        }
         if (lane == 0) {
             scale[b] = ldexpf(1.0f, e);
             xsum[b] = s;
@@ -101,28 +155,16 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
     }
 }
 
-// ---------------------------------------------------------------------------
-// GEMV.  A CTA of 8 warps works on one 16-row tile at a time; warp w takes
-// groups w, w + 8, ... of the tile and the warps combine their partial rows
-// through shared memory.  Tiles come from a queue (first one static, then an
-// atomic counter that xprep_kernel zeroes), so CTAs that finish early take
-// more work instead of idling at the tail.  Each warp keeps DRAM busy ahead
-// of its loads with one bulk L2 prefetch per group (cp.async.bulk.prefetch:
-// no registers, no completion to track) for the groups it will read next.
-// ---------------------------------------------------------------------------
-constexpr int kWarps = 8;
-constexpr int kGemvThreads = kWarps * 32;
-constexpr int kPrefetch = 3;  // groups ahead per warp
-
 struct GemvArgs {
     const uint8_t* W;
-    const uint4* frags;   // x digits, 64 x 16 B per group
-    const float* scale;   // per 32-value block
+    const uint8_t* frags;
+    const uint8_t* zeros;
+    const float* scale;
     const float* xsum;
     float* y;
-    int* queue;           // tile counter, zeroed by xprep
-    int64_t N, K;
-    int64_t ntiles, ngroups;
+    int* count;
+    float* partial;
+    int64_t ngroups, units, nwarps;
 };
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
@@ -135,14 +177,15 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
+// first warp of the split whose range holds unit u
+__device__ __forceinline__ int64_t warp_of(int64_t u, int64_t U, int64_t NW) { return ((u + 1) * NW + U - 1) / U - 1; }
 
 // One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
-// bA / bB are this lane's B registers; only their owning lanes ever load them,
-// so elsewhere they stay zero without being cleared per chunk.
+// fb: this lane's B slot of chunk 0 (or the zero slot), fc: bytes between chunks.
 template <int TYPE>
-__device__ __forceinline__ void group_dot(const uint8_t* gb, const uint4* __restrict__ fg, const float* __restrict__ sc_,
-                                          const float* __restrict__ xs_, int lane, int g, int t, bool ldA, bool ldB,
-                                          uint4& bA, uint4& bB, float& y0, float& y8) {
+__device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
+                                          const float* __restrict__ xs_, int lane, int g, int t, float& y0,
+                                          float& y8) {
     uint4 A[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
@@ -159,26 +202,27 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint4* __rest
     for (int p = 0; p < 3; ++p)
 #pragma unroll
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
-    // x digits of all eight chunks first (independent registers, so the
-    // loads overlap); only the 8 owning lanes load, the rest keep zeros
-    fg += g;
-    uint4 bf[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) bf[c] = (ldA || ldB) ? __ldg(fg + c * 8) : make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
         const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
-        const uint32_t a0 = w0 & 0x0F0F0F0Fu, a1 = (w0 >> 4) & 0x0F0F0F0Fu;
-        const uint32_t a2 = w1 & 0x0F0F0F0Fu, a3 = (w1 >> 4) & 0x0F0F0F0Fu;
-        mma_u8s8(C[0], a0, a1, a2, a3, ldA ? bf[c].x : 0u, ldB ? bf[c].x : 0u);
-        mma_u8s8(C[1], a0, a1, a2, a3, ldA ? bf[c].y : 0u, ldB ? bf[c].y : 0u);
-        mma_u8s8(C[2], a0, a1, a2, a3, ldA ? bf[c].z : 0u, ldB ? bf[c].z : 0u);
+        // rows g+8 stay in the high nibble: A = 16 q, undone in the combine below
+        const uint32_t a0 = w0 & 0x0F0F0F0Fu, a1 = w0 & 0xF0F0F0F0u;
+        const uint32_t a2 = w1 & 0x0F0F0F0Fu, a3 = w1 & 0xF0F0F0F0u;
+        mma_u8s8(C[0], a0, a1, a2, a3, q.x, q.y);
+        mma_u8s8(C[1], a0, a1, a2, a3, q.z, q.w);
+        mma_u8s8(C[2], a0, a1, a2, a3, r.x, r.y);
     }
     // C[p][0]: (row g, block 2t)  [1]: (g, 2t+1)  [2]: (g+8, 2t)  [3]: (g+8, 2t+1).
-    // |D2| <= 64, so the combined integer fits int32: 32 * 15 * (64 * 65536 + 128 * 257) < 2^31.
+    // Rows g: |sum| <= 32 * 15 * (64 * 65536 + 128 * 257) < 2^31.  Rows g+8
+    // carry a factor 16 in every plane (C0 a multiple of 16, so >> 4 is exact);
+    // |C2| <= 32 * 240 * 64, so C2 * 4096 < 2^31 as well.
     float T[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) T[k] = static_cast<float>(C[2][k] * 65536 + C[1][k] * 256 + C[0][k]);
+    T[0] = static_cast<float>(C[2][0] * 65536 + C[1][0] * 256 + C[0][0]);
+    T[1] = static_cast<float>(C[2][1] * 65536 + C[1][1] * 256 + C[0][1]);
+    T[2] = static_cast<float>(C[2][2] * 4096 + C[1][2] * 16 + (C[0][2] >> 4));
+    T[3] = static_cast<float>(C[2][3] * 4096 + C[1][3] * 16 + (C[0][3] >> 4));
     const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     const float2 xs2 = __ldg(reinterpret_cast<const float2*>(xs_) + t);
     const float s0 = sc2.x, s1 = sc2.y, x0 = xs2.x, x1 = xs2.y;
@@ -212,59 +256,77 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint4* __rest
 }
 
 template <int TYPE>
-__global__ void __launch_bounds__(kGemvThreads, 3) gemv_mma_kernel(const GemvArgs a) {
-    __shared__ float red[kWarps][MMA_TILE_ROWS];
-    __shared__ int64_t next_tile;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t tile_bytes = a.ngroups * MMA_GROUP_BYTES;
-    const bool bsrc = (g & 3) == t;  // this lane supplies a B (x digit) fragment
-    const bool ldA = bsrc && g < 4, ldB = bsrc && g >= 4;
-    uint4 bA = make_uint4(0, 0, 0, 0), bB = make_uint4(0, 0, 0, 0);
-
-    // the first tile is static: start its weights towards L2 before waiting on xprep
-    int64_t tile = blockIdx.x;
-    if (lane == 0 && tile < a.ntiles)
-        for (int d = 0; d < kPrefetch; ++d) {
-            const int64_t gi = warp + int64_t(d) * kWarps;
-            if (gi < a.ngroups) prefetch_l2(a.W + tile * tile_bytes + gi * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
-        }
+__global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(const GemvArgs a) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int64_t U = a.units, NW = a.nwarps, ng = a.ngroups;
+    const int64_t w = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+    const int64_t u0 = w < NW ? w * U / NW : 0, u1 = w < NW ? (w + 1) * U / NW : 0;
+    // start this warp's first weights towards L2 before waiting on xprep
+    if (lane == 0)
+        for (int64_t d = 0; d < kPrefetch && u0 + d < u1; ++d)
+            prefetch_l2(a.W + (u0 + d) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
     pdl_release();
-    pdl_wait();  // x digits and the tile queue come from xprep_kernel
+    pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel
 
-    while (tile < a.ntiles) {  // `tile` is CTA-uniform, so every thread runs the same iterations
-        if (threadIdx.x == 0) next_tile = static_cast<int64_t>(gridDim.x) + atomicAdd(a.queue, 1);
-        const uint8_t* tb = a.W + tile * tile_bytes;
+    const bool supplier = g == t || g == t + 4;
+    const uint8_t* fb0 = supplier ? a.frags + g * kSlotBytes : a.zeros;
+    const int fc = supplier ? kChunkFragBytes : 0;
+    const int64_t fg = supplier ? kGroupFragBytes : 0;
+    int64_t u = u0;
+    while (u < u1) {
+        const int64_t tile = u / ng, tbeg = tile * ng;
+        const int64_t gend = (u1 - tbeg) < ng ? (u1 - tbeg) : ng;
         float y0 = 0.f, y8 = 0.f;
-        for (int64_t gi = warp; gi < a.ngroups; gi += kWarps) {
-            const int64_t ahead = gi + int64_t(kPrefetch) * kWarps;
-            if (lane == 0 && ahead < a.ngroups) prefetch_l2(tb + ahead * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
-            group_dot<TYPE>(tb + gi * MMA_GROUP_BYTES, a.frags + gi * 64, a.scale + gi * 8, a.xsum + gi * 8, lane, g,
-                            t, ldA, ldB, bA, bB, y0, y8);
+        for (int64_t gi = u - tbeg; gi < gend; ++gi) {
+            const int64_t ua = tbeg + gi;
+            if (lane == 0 && ua + kPrefetch < u1) prefetch_l2(a.W + (ua + kPrefetch) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+            group_dot<TYPE>(a.W + ua * MMA_GROUP_BYTES, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g,
+                            t, y0, y8);
         }
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
         y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
         y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
-        if (t == 0) {
-            red[warp][g] = y0;
-            red[warp][g + 8] = y8;
-        }
-        __syncthreads();
-        const int64_t nt = next_tile;
-        if (threadIdx.x < MMA_TILE_ROWS) {
-            float acc = 0.f;
-            const int nw = static_cast<int>(a.ngroups < kWarps ? a.ngroups : kWarps);
-            for (int w = 0; w < nw; ++w) acc += red[w][threadIdx.x];
-            a.y[tile * MMA_TILE_ROWS + threadIdx.x] = acc;
-        }
-        // warm L2 with the next tile's first groups of this warp
-        if (lane == 0 && nt < a.ntiles)
-            for (int d = 0; d < kPrefetch; ++d) {
-                const int64_t gi = warp + int64_t(d) * kWarps;
-                if (gi < a.ngroups) prefetch_l2(a.W + nt * tile_bytes + gi * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+        if (u == tbeg && gend == ng) {  // the whole tile is this warp's
+            if (t == 0) {
+                a.y[tile * MMA_TILE_ROWS + g] = y0;
+                a.y[tile * MMA_TILE_ROWS + g + 8] = y8;
             }
-        __syncthreads();
-        tile = nt;
+        } else {
+            float* mine = a.partial + (w * 2 + (u == u0 ? 0 : 1)) * MMA_TILE_ROWS;
+            if (t == 0) {
+                mine[g] = y0;
+                mine[g + 8] = y8;
+            }
+            __threadfence();
+            __syncwarp();
+            int prev = 0;
+            if (lane == 0) prev = atomicAdd(a.count + tile, 1);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            const int64_t wa = warp_of(tbeg, U, NW), wb = warp_of(tbeg + ng - 1, U, NW);
+            if (prev == static_cast<int>(wb - wa)) {  // last contributor
+                __threadfence();
+                // lane (row r, half h) adds contributors wa + h, wa + h + 2, ...
+                // in a fixed order, eight independent loads in flight at a time
+                const int r = lane & 15, h = lane >> 4;
+                const int slot_a = (wa * U / NW < tbeg) ? 1 : 0;  // wa's last tile, else its first
+                float acc = 0.f;
+                for (int64_t v0 = wa + h; v0 <= wb; v0 += 16) {
+                    float part[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int64_t v = v0 + 2 * j;
+                        const int slot = v == wa ? slot_a : 0;
+                        part[j] = v <= wb ? __ldcg(a.partial + (v * 2 + slot) * MMA_TILE_ROWS + r) : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc += part[j];
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+                if (h == 0) a.y[tile * MMA_TILE_ROWS + r] = acc;
+            }
+        }
+        u = tbeg + gend;
     }
 }
 
@@ -374,19 +436,19 @@ int g_scratch_n = 0;
 
 }  // namespace
 
-// Scratch of one MMA GEMV launch: x digits (1 KiB per 256 values), block
-// scales and sums (per 32 values) and the tile queue counter, which
-// xprep_kernel zeroes at the start of every launch.
+// Scratch of one MMA GEMV launch (layout described above the kernels).
 ScratchLayout scratch_layout(int64_t N, int64_t K) {
-    (void)N;
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     ScratchLayout L;
-    const int64_t ngroups = K / 256;
+    const size_t ngroups = static_cast<size_t>(K / 256), nblk = static_cast<size_t>(K / 32);
+    const size_t ntiles = static_cast<size_t>(N / MMA_TILE_ROWS);
     L.frags = 0;
-    L.scale = up(L.frags + static_cast<size_t>(ngroups) * 1024);
-    L.xsum = up(L.scale + static_cast<size_t>(K / 32) * sizeof(float));
-    L.queue = up(L.xsum + static_cast<size_t>(K / 32) * sizeof(float));
-    L.total = up(L.queue + sizeof(int));
+    L.zeros = up(L.frags + ngroups * kGroupFragBytes);
+    L.scale = up(L.zeros + kSlotBytes);
+    L.xsum = up(L.scale + nblk * sizeof(float));
+    L.count = up(L.xsum + nblk * sizeof(float));
+    L.partial = up(L.count + ntiles * sizeof(int));
+    L.total = up(L.partial + size_t(kMaxCtas) * kWarps * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
 }
 
@@ -408,19 +470,21 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
 
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
                             void* scratch, cudaStream_t stream, bool pdl) {
+    if (type != T_Q4_K && type != T_Q4_0) return cudaErrorInvalidValue;
     const ScratchLayout L = scratch_layout(N, K);
     uint8_t* base = static_cast<uint8_t*>(scratch);
+    const int64_t ntiles = N / MMA_TILE_ROWS, ngroups = K / 256, nblk = K / 32;
     GemvArgs a;
     a.W = static_cast<const uint8_t*>(W);
-    a.frags = reinterpret_cast<const uint4*>(base + L.frags);
+    a.frags = base + L.frags;
+    a.zeros = base + L.zeros;
     a.scale = reinterpret_cast<const float*>(base + L.scale);
     a.xsum = reinterpret_cast<const float*>(base + L.xsum);
     a.y = y;
-    a.queue = reinterpret_cast<int*>(base + L.queue);
-    a.N = N;
-    a.K = K;
-    a.ntiles = N / MMA_TILE_ROWS;
-    a.ngroups = K / 256;
+    a.count = reinterpret_cast<int*>(base + L.count);
+    a.partial = reinterpret_cast<float*>(base + L.partial);
+    a.ngroups = ngroups;
+    a.units = ntiles * ngroups;
 
     static int s_sms[16] = {};
     int dev = 0;
@@ -428,24 +492,31 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
     if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
     if (s_sms[dev] == 0) cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     const int sms = s_sms[dev] > 0 ? s_sms[dev] : 148;
+    int64_t blocks = int64_t(sms) * kCtasPerSm;
+    if (blocks > kMaxCtas) blocks = kMaxCtas;
+    if (blocks > (a.units + kWarps - 1) / kWarps) blocks = (a.units + kWarps - 1) / kWarps;
+    if (blocks < 1) blocks = 1;
+    a.nwarps = blocks * kWarps < a.units ? blocks * kWarps : a.units;
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cudaLaunchConfig_t cp = {};
-    const int64_t nblk = K / 32;
-    cp.gridDim = dim3(static_cast<unsigned>((nblk + 1) / 2));  // one warp per 32-value block
+    int64_t xblocks = (nblk + 1) / 2;                       // one warp per 32-value block
+    if ((ntiles + 63) / 64 > xblocks) xblocks = (ntiles + 63) / 64;  // and a thread per tile counter
+    if (xblocks > 4096) xblocks = 4096;
+    cp.gridDim = dim3(static_cast<unsigned>(xblocks));
     cp.blockDim = dim3(64);
     cp.stream = stream;
     cp.attrs = attr;
     cp.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, base + L.frags, reinterpret_cast<float*>(base + L.scale),
-                                       reinterpret_cast<float*>(base + L.xsum), a.queue);
+    cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, base + L.frags, base + L.zeros,
+                                       reinterpret_cast<float*>(base + L.scale),
+                                       reinterpret_cast<float*>(base + L.xsum), a.count, ntiles);
     if (e != cudaSuccess) return e;
 
-    int64_t blocks = a.ntiles < int64_t(sms) * 3 ? a.ntiles : int64_t(sms) * 3;
     cudaLaunchConfig_t cg = {};
-    cg.gridDim = dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks));
+    cg.gridDim = dim3(static_cast<unsigned>(blocks));
     cg.blockDim = dim3(kGemvThreads);
     cg.stream = stream;
     cudaLaunchAttribute attr2[1];
@@ -454,8 +525,7 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
     cg.attrs = attr2;
     cg.numAttrs = 1;
     if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
-    if (type == T_Q4_0) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
-    return cudaErrorInvalidValue;
+    return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
 // Scratch for launcher calls that bring none: two slots per (device, stream),

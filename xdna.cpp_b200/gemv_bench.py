@@ -111,11 +111,12 @@ def bench_one(torch, name: str, n: int, k: int, iters: int, warmup: int, graph: 
         with torch.cuda.graph(g, stream=s):
             for i in range(iters):
                 launch(i)
-        g.replay()
-        torch.cuda.synchronize()
-        e0.record(s)
-        g.replay()
-        e1.record(s)
+        with torch.cuda.stream(s):
+            g.replay()
+            torch.cuda.synchronize()
+            e0.record(s)
+            g.replay()
+            e1.record(s)
     else:
         e0.record(s)
         for i in range(iters):

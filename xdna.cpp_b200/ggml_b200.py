@@ -15,7 +15,9 @@ import re
 from functools import lru_cache
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libggml-b200.so")
+# XDNA_B200_LIB selects another build of the library (the role GGML_BACKEND_PATH
+# plays for a ggml host); the default is the in-tree build.
+LIB_PATH = os.environ.get("XDNA_B200_LIB") or os.path.join(HERE, "libggml-b200.so")
 HEADER = os.path.join(HERE, "..", "include", "ggml-b200.h")
 
 # ggml type ids
