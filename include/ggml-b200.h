@@ -162,6 +162,21 @@ size_t ggml_backend_xdna_get_device_count(void);
  * XdnaGemvEngine::run / run_quant (src/xdna-gemv-engine.cpp:1817-1992). */
 int b200_gemv(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
               void *stream, int pdl);
+/* b200_gemv that allocates no device memory.  No reference counterpart (the
+ * reference's CPU path needs no device scratch).  It is for callers that
+ * cannot allocate device memory at call time: a host that has handed all
+ * device memory to its own pools, or a decode loop that cannot take the
+ * device-wide synchronisation of cudaMalloc / cudaFree in the middle of a
+ * token.  The Q4_0 / Q4_K MMA path (N % 16 == 0, K % 256 == 0) then uses a
+ * fixed 1 MiB static device array for its scratch instead of the per-stream
+ * buffers b200_gemv grows on demand; shapes needing more (above N = 131072
+ * with K = 32768) fail with an error naming the limit.  The other formats
+ * need no scratch and run as in b200_gemv.  The array's device address is
+ * looked up (cudaGetSymbolAddress) by the first call on each device, so make
+ * that first call before capturing a stream.  The array is shared by every
+ * stream of the device: calls whose executions overlap in time race. */
+int b200_gemv_noalloc(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
+                      void *stream);
 /* GGUF rows -> stripe layout (out of place), the GPU replacement of the
  * reference's Q4Prepacker::pack (src/xdna-q4-prepack.cpp:39-114). */
 int b200_repack(int type, const void *raw, void *packed, int64_t n, int64_t k, void *stream);

@@ -1251,6 +1251,40 @@ int b200_gemv(int type, const void* w_packed, const float* x, float* y, int64_t 
     return launch_rc(gemv_launch(type, w_packed, x, y, n, k, static_cast<cudaStream_t>(stream), lo), "b200_gemv");
 }
 
+// b200_gemv without device allocation (see the declaration): the MMA path
+// gets the static-array scratch instead of launcher_scratch's buffers.
+int b200_gemv_noalloc(int type, const void* w_packed, const float* x, float* y, int64_t n, int64_t k, void* stream) {
+    const FormatInfo f = format_info(type);
+    if (!f.block_vals || k < 0 || k % f.block_vals || n < 0) {
+        set_error("b200_gemv_noalloc: bad type %d / shape N=%ld K=%ld", type, long(n), long(k));
+        return -1;
+    }
+    if (n > 0 && (!w_packed || !x || !y)) {
+        set_error("b200_gemv_noalloc: null pointer");
+        return -1;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15u) {
+        set_error("b200_gemv_noalloc: x must be 16-byte aligned");
+        return -1;
+    }
+    LaunchOpts lo;
+    if (n > 0 && layout_kind(type, n, k) == 1) {
+        const size_t need = xprep_bytes(n, k);
+        if (need > static_scratch_bytes()) {
+            set_error("b200_gemv_noalloc: N=%ld K=%ld needs %zu bytes of scratch, more than its fixed %zu-byte "
+                      "area (fits N <= 131072 with K <= 32768); use b200_gemv",
+                      long(n), long(k), need, static_scratch_bytes());
+            return -1;
+        }
+        void* s = nullptr;
+        const cudaError_t e = static_scratch(&s);
+        if (e != cudaSuccess) return launch_rc(e, "b200_gemv_noalloc: cudaGetSymbolAddress");
+        lo.scratch = s;
+    }
+    return launch_rc(gemv_launch(type, w_packed, x, y, n, k, static_cast<cudaStream_t>(stream), lo),
+                     "b200_gemv_noalloc");
+}
+
 int b200_repack(int type, const void* raw, void* packed, int64_t n, int64_t k, void* stream) {
     return launch_rc(repack_launch(type, raw, packed, n, k, 0, n, static_cast<cudaStream_t>(stream)), "b200_repack");
 }

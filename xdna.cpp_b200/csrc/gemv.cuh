@@ -20,6 +20,10 @@ struct ScratchLayout {
 ScratchLayout scratch_layout(int64_t N, int64_t K);
 size_t xprep_bytes(int64_t N, int64_t K);
 void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K);
+// The fixed static-array scratch of b200_gemv_noalloc: its size, and its
+// device address on the current device (cudaGetSymbolAddress, once per device).
+size_t static_scratch_bytes();
+cudaError_t static_scratch(void** out);
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K, void* scratch,
                             cudaStream_t stream, bool pdl);
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,

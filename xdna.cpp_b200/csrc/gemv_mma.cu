@@ -528,6 +528,36 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
+// Fixed scratch of b200_gemv_noalloc: one static device array per device
+// instead of buffers allocated on demand.  1 MiB holds the layout above for
+// N <= 131072 rows with K <= 32768 (frags 256 KiB, counters 32 KiB, partial
+// slots 512 KiB, scales and sums 8 KiB).  Nothing in it has to start zeroed:
+// every launch's xprep_kernel writes the digits and clears the tile counters
+// before the GEMV reads them.  It is shared by every stream of the device.
+static __device__ __align__(256) unsigned char g_static_scratch[size_t(1) << 20];
+
+size_t static_scratch_bytes() { return sizeof(g_static_scratch); }
+
+// Device address of g_static_scratch on the current device, looked up once
+// per device (cudaGetSymbolAddress) and cached.
+cudaError_t static_scratch(void** out) {
+    static std::mutex m;
+    static void* addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(m);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
 // Scratch for launcher calls that bring none: two slots per (device, stream),
 // alternated so that a GEMV reading one slot can overlap (PDL) the next call's
 // x preparation writing the other.  Grown on demand (must not happen inside
