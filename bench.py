@@ -54,6 +54,7 @@ def row_bytes_q4k(K: int) -> int:
 WEIGHT_BYTES_PER_TOKEN = (LAYERS * sum(N * row_bytes_q4k(K) for _, N, K in LAYER_MATS)
                           + VOCAB * row_bytes_q4k(HIDDEN))
 MATMULS_PER_TOKEN = LAYERS * len(LAYER_MATS) + 1
+LAUNCHES_PER_TOKEN = LAYERS * 4 + 1  # q/k/v fused, o, gate/up fused, down; lm_head
 
 
 # ------------------------------------------------------------------ plumbing
@@ -341,23 +342,34 @@ def be_last_error() -> str:
 
 
 def kernel_only_ms(torch, G, model, steps: int) -> float:
-    """Time of the step's 561 local GEMV launches alone (no collectives), for
-    the roofline of the dominant kernel."""
+    """Device time of one step's GEMV launches alone (no collectives, no
+    host work): the launches compute_graph makes -- q/k/v and gate/up fused
+    (b200_gemv_multi), o, down and lm_head single (b200_gemv) -- captured once
+    as a CUDA graph and replayed, for the roofline of the dominant kernel."""
+    import ctypes as C
+
     a = model.act
-    plan = []
+    plan = []  # (weights, outputs, rows, x, K) per launch
+    groups = [(("q", "k", "v"), "h"), (("o",), "q"), (("gate", "up"), "o"), (("down",), "gate")]
     for layer in range(LAYERS):
-        for name, N, K in LAYER_MATS:
-            x = {"q": "h", "k": "h", "v": "h", "o": "q", "gate": "o", "up": "o", "down": "gate"}[name]
-            y = {"down": "h"}.get(name, name)
-            w = model.weights[(layer, name)]
-            plan.append((w.data, a[x].data_ptr(), a[y].data_ptr(), w.ne[1], K))
+        for names, x in groups:
+            ws = [model.weights[(layer, n)] for n in names]
+            ys = [a[{"down": "h"}.get(n, n)].data_ptr() for n in names]
+            plan.append(([w.data for w in ws], ys, [w.ne[1] for w in ws], a[x].data_ptr(), ws[0].ne[0]))
     w = model.weights[(LAYERS, "lm_head")]
-    plan.append((w.data, a["h"].data_ptr(), a["logits"].data_ptr(), w.ne[1], HIDDEN))
+    plan.append(([w.data], [a["logits"].data_ptr()], [w.ne[1]], a["h"].data_ptr(), HIDDEN))
     L = G.lib()
+    packed = []
+    for wps, yps, ns, xp, k in plan:
+        n = len(wps)
+        packed.append((n, (C.c_void_p * n)(*wps), (C.c_void_p * n)(*yps), (C.c_int64 * n)(*ns), xp, k))
 
     def step(stream_handle: int):
-        for wp, xp, yp, n, k in plan:
-            rc = L.b200_gemv(Q4_K, wp, xp, yp, n, k, stream_handle, 0)
+        for n, wps, yps, ns, xp, k in packed:
+            if n == 1:
+                rc = L.b200_gemv(Q4_K, wps[0], xp, yps[0], ns[0], k, stream_handle, 1)
+            else:
+                rc = L.b200_gemv_multi(Q4_K, wps, yps, ns, n, xp, k, stream_handle, 1)
             if rc:
                 raise RuntimeError(G.last_error())
 
@@ -452,11 +464,12 @@ def run_b200_arm(args, dist: Dist) -> None:
             "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<12> (Q4_K) with its xprep_kernel",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": None, "per_launch_note": "561 launches per step; achieved = local weight bytes "
-                         "per step / GEMV-only device time per step"},
+                         "traffic": None, "per_launch_note": f"{LAUNCHES_PER_TOKEN} GEMV launches per step (q/k/v and gate/up "
+                         "fused); achieved = local weight bytes per step / GEMV-only device time per step"},
             "clocks": clk.summary(),
-            # per MUL_MAT: xprep_kernel + gemv_mma_kernel (NCCL's all-gather kernels not counted)
-            "gpu_launches": args.steps * MATMULS_PER_TOKEN * 2,
+            # per launch group (q/k/v and gate/up fused, o, down, lm_head):
+            # xprep_kernel + gemv_mma_kernel; NCCL's all-gather kernels not counted
+            "gpu_launches": args.steps * LAUNCHES_PER_TOKEN * 2,
         }
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}

@@ -162,6 +162,13 @@ size_t ggml_backend_xdna_get_device_count(void);
  * XdnaGemvEngine::run / run_quant (src/xdna-gemv-engine.cpp:1817-1992). */
 int b200_gemv(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
               void *stream, int pdl);
+/* y_s = W_s x for up to 4 matrices that share x (q / k / v or gate / up of a
+ * transformer block) in one x preparation and one GEMV launch.  Every W_s must
+ * be in the 16-row MMA layout (Q4_0 / Q4_K, N_s % 16 == 0, K % 256 == 0).  No
+ * reference counterpart; ggml_backend_xdna_compute_graph applies the same
+ * fusion to consecutive nodes that qualify. */
+int b200_gemv_multi(int type, const void *const *w_packed, float *const *y, const int64_t *n, int nseg,
+                    const float *x, int64_t k, void *stream, int pdl);
 /* b200_gemv that allocates no device memory.  No reference counterpart (the
  * reference's CPU path needs no device scratch).  It is for callers that
  * cannot allocate device memory at call time: a host that has handed all

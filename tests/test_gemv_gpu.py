@@ -321,3 +321,35 @@ def test_mma_split_shapes_interleaved_and_deterministic(cuda, G, O):
                 first[i] = y
             else:
                 np.testing.assert_array_equal(y, first[i])
+
+
+def test_compute_graph_fuses_nodes_sharing_x(cuda, G, O):
+    """q / k / v (and gate / up) style nodes: consecutive MUL_MATs on one
+    device-resident x with resident MMA-layout weights run as one fused
+    launch; each output matches the oracle, and so does a node that consumes
+    a fused output (it must not be fused with its producers)."""
+    K = 2048
+    shapes = [(2048, G.Q4_K), (256, G.Q4_K), (256, G.Q4_K), (512, G.Q4_K)]  # q, k, v, then o reads q
+    raws = [O.quantize(t, normal_weights(N, K, seed=60 + i)) for i, (N, t) in enumerate(shapes)]
+    x = normal_x(K, seed=61)
+    with G.Backend(0) as be:
+        buf = G.Buffer(sum(r.nbytes for r in raws) + 8 * 8192, dev=0)
+        ws = []
+        for (N, t), raw in zip(shapes, raws):
+            w = buf.alloc(G.tensor(t, [K, N, 1, 1]))
+            buf.set(w, _np_ptr(raw), 0, raw.nbytes)
+            ws.append(w)
+        d_x = to_dev(cuda, x)
+        ys = [cuda.full((N,), float("nan"), dtype=cuda.float32, device="cuda") for N, _ in shapes]
+        xt = G.tensor(G.F32, [K, 1, 1, 1], data=d_x.data_ptr())
+        qt = G.tensor(G.F32, [K, 1, 1, 1], data=ys[0].data_ptr())  # o's input: q's output (N_q == K)
+        nodes = [G.mul_mat_node(ws[i], xt, ys[i].data_ptr(), shapes[i][0], name=f"n{i}") for i in range(3)]
+        nodes.append(G.mul_mat_node(ws[3], qt, ys[3].data_ptr(), shapes[3][0], name="o"))
+        for rep in range(2):
+            assert be.compute(nodes), G.last_error()
+            be.synchronize()
+            got = [y.cpu().numpy() for y in ys]
+            for i in range(3):
+                check_parity(got[i], O.gemv(shapes[i][1], raws[i], shapes[i][0], K, x), f"fused node {i} rep {rep}")
+            check_parity(got[3], O.gemv(G.Q4_K, raws[3], shapes[3][0], K, got[0]), f"consumer rep {rep}")
+        buf.free()

@@ -754,6 +754,7 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
                     if (!yd) return false;
                 }
                 LaunchOpts lo;
+                lo.pdl = true;  // kernels wait (griddepcontrol) before touching what earlier work writes
                 if (layout_kind(src0->type, N, K) == 1) {
                     lo.scratch = backend_xscratch(be, N, K);
                     if (!lo.scratch) return false;
@@ -771,6 +772,92 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
             }
         }
     }
+    return true;
+}
+
+// ------------------------------------------------------------- node fusion
+// Consecutive MUL_MAT nodes that multiply the same device-resident x by
+// MMA-layout weights (q / k / v, or gate / up, of a transformer block) run as
+// one launch: one x preparation, one GEMV grid over all their row tiles.
+struct FusableNode {
+    int type;
+    int64_t K;
+    const float* x;
+    MmaSegment seg;   // W, this rank's output rows, local N
+    float* y_full;    // the node's output (all ranks' rows when sharded)
+    int64_t n_out;    // rows of y_full
+    bool sharded;
+};
+
+bool fusable(Backend* be, const ggml_tensor_xdna* node, FusableNode* out) {
+    if (!node || node->op != GGML_OP_MUL_MAT) return false;
+    const ggml_tensor_xdna* src0 = node->src[0];
+    const ggml_tensor_xdna* src1 = node->src[1];
+    if (!src0 || !src1 || src1->type != GGML_TYPE_F32 || !node->data || !src0->data || !src1->data) return false;
+    const int64_t K = src0->ne[0], N = src0->ne[1];
+    if (src1->ne[1] != 1 || src1->ne[0] != K || layout_kind(src0->type, N, K) != 1) return false;
+    for (int d = 2; d < 4; ++d)
+        if (node->ne[d] > 1 || src0->ne[d] > 1 || src1->ne[d] > 1) return false;
+    const size_t rb = static_cast<size_t>(K / 256) * 144;
+    if (src0->nb[1] != 0 && src0->nb[1] != rb) return false;
+    if ((reinterpret_cast<uintptr_t>(src1->data) & 15u) || !is_device_pointer(src1->data) ||
+        !is_device_pointer(node->data))
+        return false;
+    Buffer* wbuf = registry().find(src0->data);
+    if (!wbuf || wbuf->buft->host || wbuf->buft->dev != be->dev) return false;
+    {
+        std::lock_guard<std::mutex> lk(wbuf->mtx);
+        auto it = wbuf->tensors.find(reinterpret_cast<uintptr_t>(src0->data));
+        if (it == wbuf->tensors.end() || !it->second.packed || it->second.N != N || it->second.K != K) return false;
+    }
+    const bool sharded = be->world > 1 && node->ne[0] == N * be->world;
+    if (!sharded && node->ne[0] != N) return false;
+    out->type = src0->type;
+    out->K = K;
+    out->x = static_cast<const float*>(src1->data);
+    out->y_full = static_cast<float*>(node->data);
+    out->n_out = sharded ? N * be->world : N;
+    out->seg = MmaSegment{src0->data, out->y_full + (sharded ? be->rank * N : 0), N};
+    out->sharded = sharded;
+    return true;
+}
+
+// Nodes [i, i + count) of `nodes` that fuse with node i (count >= 1 when node i is fusable).
+size_t fused_run_length(Backend* be, ggml_tensor_xdna** nodes, size_t i, size_t n_nodes, FusableNode* f) {
+    if (!fusable(be, nodes[i], &f[0])) return 0;
+    const char* x0 = reinterpret_cast<const char*>(f[0].x);
+    const size_t xbytes = static_cast<size_t>(f[0].K) * sizeof(float);
+    auto overlaps = [](const void* a, size_t an, const void* b, size_t bn) {
+        return static_cast<const char*>(a) < static_cast<const char*>(b) + bn &&
+               static_cast<const char*>(b) < static_cast<const char*>(a) + an;
+    };
+    if (overlaps(f[0].y_full, f[0].n_out * 4, x0, xbytes)) return 1;
+    size_t n = 1;
+    while (n < static_cast<size_t>(MMA_MAX_SEGMENTS) && i + n < n_nodes) {
+        FusableNode c;
+        if (!fusable(be, nodes[i + n], &c) || c.type != f[0].type || c.K != f[0].K || c.x != f[0].x) break;
+        bool clash = overlaps(c.y_full, c.n_out * 4, x0, xbytes);
+        for (size_t k = 0; k < n && !clash; ++k) clash = overlaps(c.y_full, c.n_out * 4, f[k].y_full, f[k].n_out * 4);
+        if (clash) break;
+        f[n++] = c;
+    }
+    return n;
+}
+
+bool run_fused(Backend* be, const FusableNode* f, size_t n) {
+    MmaSegment segs[MMA_MAX_SEGMENTS];
+    int64_t rows = 0;
+    for (size_t k = 0; k < n; ++k) {
+        segs[k] = f[k].seg;
+        rows += f[k].seg.N;
+    }
+    void* scratch = backend_xscratch(be, rows, f[0].K);
+    if (!scratch) return false;
+    if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true),
+                 "fused gemv launch"))
+        return false;
+    for (size_t k = 0; k < n; ++k)
+        if (f[k].sharded && !all_gather_rows(be, f[k].y_full, f[k].seg.N)) return false;
     return true;
 }
 
@@ -923,15 +1010,23 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
     std::lock_guard<std::mutex> lk(be->mtx);
     DeviceGuard g(be->dev);
     static const bool trace = getenv("XDNA_TRACE_NODES") != nullptr;
+    static const bool no_fuse = getenv("XDNA_NO_FUSE") != nullptr;
     bool ok = true;
-    for (size_t i = 0; i < n_nodes && ok; ++i) {
+    for (size_t i = 0; i < n_nodes && ok;) {
         ggml_tensor_xdna* node = nodes[i];
-        if (!node || node->op != GGML_OP_MUL_MAT) continue;
-        ok = run_node(be, node);
-        if (trace && ok && node->src[0])
-            fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued\n", i,
-                    node->name[0] ? node->name : "unnamed", node->src[0]->type, long(node->src[0]->ne[1]),
-                    long(node->src[0]->ne[0]));
+        if (!node || node->op != GGML_OP_MUL_MAT) {
+            ++i;
+            continue;
+        }
+        FusableNode f[MMA_MAX_SEGMENTS];
+        const size_t run = no_fuse ? 0 : fused_run_length(be, nodes, i, n_nodes, f);
+        const size_t count = run > 1 ? run : 1;
+        ok = run > 1 ? run_fused(be, f, run) : run_node(be, node);
+        for (size_t k = i; trace && ok && k < i + count; ++k)
+            fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued%s\n", k,
+                    nodes[k]->name[0] ? nodes[k]->name : "unnamed", nodes[k]->src[0]->type,
+                    long(nodes[k]->src[0]->ne[1]), long(nodes[k]->src[0]->ne[0]), count > 1 ? " (fused)" : "");
+        i += count;
     }
     const bool flushed = flush(be);
     return ok && flushed;
@@ -1249,6 +1344,34 @@ int b200_gemv(int type, const void* w_packed, const float* x, float* y, int64_t 
     LaunchOpts lo;
     lo.pdl = pdl != 0;
     return launch_rc(gemv_launch(type, w_packed, x, y, n, k, static_cast<cudaStream_t>(stream), lo), "b200_gemv");
+}
+
+int b200_gemv_multi(int type, const void* const* w_packed, float* const* y, const int64_t* n, int nseg, const float* x,
+                    int64_t k, void* stream, int pdl) {
+    if (nseg < 1 || nseg > MMA_MAX_SEGMENTS || !w_packed || !y || !n || !x) {
+        set_error("b200_gemv_multi: bad segment list (1..%d matrices)", MMA_MAX_SEGMENTS);
+        return -1;
+    }
+    if (reinterpret_cast<uintptr_t>(x) & 15u) {
+        set_error("b200_gemv_multi: x must be 16-byte aligned");
+        return -1;
+    }
+    MmaSegment segs[MMA_MAX_SEGMENTS];
+    int64_t rows = 0;
+    for (int s = 0; s < nseg; ++s) {
+        if (!w_packed[s] || !y[s] || layout_kind(type, n[s], k) != 1) {
+            set_error("b200_gemv_multi: matrix %d (type %d, N=%ld, K=%ld) is not in the 16-row MMA layout "
+                      "(Q4_0 / Q4_K, N %% 16 == 0, K %% 256 == 0)",
+                      s, type, long(n[s]), long(k));
+            return -1;
+        }
+        segs[s] = MmaSegment{w_packed[s], y[s], n[s]};
+        rows += n[s];
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* scratch = launcher_scratch(st, rows, k);
+    if (!scratch) return launch_rc(cudaErrorMemoryAllocation, "b200_gemv_multi scratch");
+    return launch_rc(gemv_mma_multi_launch(type, segs, nseg, x, k, scratch, st, pdl != 0), "b200_gemv_multi");
 }
 
 // b200_gemv without device allocation (see the declaration): the MMA path

@@ -344,6 +344,7 @@ XB_HD void unrepack_one(const Geometry& g, int tr, int r, int64_t b, const uint8
 //         (the blocks whose C columns lane (g, t) owns).
 // ---------------------------------------------------------------------------
 constexpr int MMA_TILE_ROWS = 16;
+constexpr int MMA_MAX_SEGMENTS = 4;  // matrices sharing x in one MMA GEMV launch
 constexpr int MMA_GROUP_BYTES = 2304;
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {

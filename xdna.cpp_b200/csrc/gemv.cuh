@@ -26,6 +26,16 @@ size_t static_scratch_bytes();
 cudaError_t static_scratch(void** out);
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K, void* scratch,
                             cudaStream_t stream, bool pdl);
+// Several MMA-layout matrices of one type that multiply the same x (same K)
+// in one launch: y_s = W_s x for s < nseg <= MMA_MAX_SEGMENTS, scratch of
+// xprep_bytes(sum of N_s, K).
+struct MmaSegment {
+    const void* W;
+    float* y;
+    int64_t N;
+};
+cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
+                                  void* scratch, cudaStream_t stream, bool pdl);
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,
                               cudaStream_t stream);
 

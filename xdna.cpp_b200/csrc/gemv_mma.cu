@@ -155,17 +155,42 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
     }
 }
 
+// One launch covers up to kMaxSegs weight matrices that share x (and K):
+// their 16-row tiles are numbered one after the other, matrix s owning tiles
+// [tile_end[s-1], tile_end[s]).
+constexpr int kMaxSegs = MMA_MAX_SEGMENTS;
+
 struct GemvArgs {
-    const uint8_t* W;
+    const uint8_t* W[kMaxSegs];
+    float* y[kMaxSegs];
+    int64_t tile_end[kMaxSegs];
+    int nseg;
     const uint8_t* frags;
     const uint8_t* zeros;
     const float* scale;
     const float* xsum;
-    float* y;
     int* count;
     float* partial;
     int64_t ngroups, units, nwarps;
 };
+
+// matrix of a (global) tile, and the tile's first byte / first output row
+__device__ __forceinline__ int seg_of(const GemvArgs& a, int64_t tile) {
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < kMaxSegs - 1; ++i) s += (i + 1 < a.nseg && tile >= a.tile_end[i]) ? 1 : 0;
+    return s;
+}
+__device__ __forceinline__ const uint8_t* tile_weights(const GemvArgs& a, int s, int64_t tile) {
+    return a.W[s] + (tile - (s ? a.tile_end[s - 1] : 0)) * a.ngroups * MMA_GROUP_BYTES;
+}
+__device__ __forceinline__ float* tile_out(const GemvArgs& a, int s, int64_t tile) {
+    return a.y[s] + (tile - (s ? a.tile_end[s - 1] : 0)) * MMA_TILE_ROWS;
+}
+__device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
+    const int64_t tile = u / a.ngroups;
+    return tile_weights(a, seg_of(a, tile), tile) + (u - tile * a.ngroups) * MMA_GROUP_BYTES;
+}
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
     uint4 v;
@@ -263,8 +288,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     const int64_t u0 = w < NW ? w * U / NW : 0, u1 = w < NW ? (w + 1) * U / NW : 0;
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
-        for (int64_t d = 0; d < kPrefetch && u0 + d < u1; ++d)
-            prefetch_l2(a.W + (u0 + d) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
+        for (int64_t d = 0; d < kPrefetch && u0 + d < u1; ++d) prefetch_l2(unit_weights(a, u0 + d), MMA_GROUP_BYTES);
     pdl_release();
     pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel
 
@@ -276,12 +300,15 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     while (u < u1) {
         const int64_t tile = u / ng, tbeg = tile * ng;
         const int64_t gend = (u1 - tbeg) < ng ? (u1 - tbeg) : ng;
+        const int seg = seg_of(a, tile);
+        const uint8_t* tw = tile_weights(a, seg, tile);
+        float* ty = tile_out(a, seg, tile);
         float y0 = 0.f, y8 = 0.f;
         for (int64_t gi = u - tbeg; gi < gend; ++gi) {
             const int64_t ua = tbeg + gi;
-            if (lane == 0 && ua + kPrefetch < u1) prefetch_l2(a.W + (ua + kPrefetch) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
-            group_dot<TYPE>(a.W + ua * MMA_GROUP_BYTES, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g,
-                            t, y0, y8);
+            if (lane == 0 && ua + kPrefetch < u1) prefetch_l2(unit_weights(a, ua + kPrefetch), MMA_GROUP_BYTES);
+            group_dot<TYPE>(tw + gi * MMA_GROUP_BYTES, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g, t,
+                            y0, y8);
         }
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
@@ -289,8 +316,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
         if (u == tbeg && gend == ng) {  // the whole tile is this warp's
             if (t == 0) {
-                a.y[tile * MMA_TILE_ROWS + g] = y0;
-                a.y[tile * MMA_TILE_ROWS + g + 8] = y8;
+                ty[g] = y0;
+                ty[g + 8] = y8;
             }
         } else {
             float* mine = a.partial + (w * 2 + (u == u0 ? 0 : 1)) * MMA_TILE_ROWS;
@@ -323,7 +350,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     for (int j = 0; j < 8; ++j) acc += part[j];
                 }
                 acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-                if (h == 0) a.y[tile * MMA_TILE_ROWS + r] = acc;
+                if (h == 0) ty[r] = acc;
             }
         }
         u = tbeg + gend;
@@ -470,17 +497,30 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
 
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
                             void* scratch, cudaStream_t stream, bool pdl) {
-    if (type != T_Q4_K && type != T_Q4_0) return cudaErrorInvalidValue;
-    const ScratchLayout L = scratch_layout(N, K);
+    const MmaSegment seg{W, y, N};
+    return gemv_mma_multi_launch(type, &seg, 1, x, K, scratch, stream, pdl);
+}
+
+cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
+                                  void* scratch, cudaStream_t stream, bool pdl) {
+    if ((type != T_Q4_K && type != T_Q4_0) || nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+    GemvArgs a = {};
+    int64_t ntiles = 0;
+    for (int s = 0; s < nseg; ++s) {
+        if (layout_kind(type, segs[s].N, K) != 1) return cudaErrorInvalidValue;
+        a.W[s] = static_cast<const uint8_t*>(segs[s].W);
+        a.y[s] = segs[s].y;
+        ntiles += segs[s].N / MMA_TILE_ROWS;
+        a.tile_end[s] = ntiles;
+    }
+    a.nseg = nseg;
+    const ScratchLayout L = scratch_layout(ntiles * MMA_TILE_ROWS, K);
     uint8_t* base = static_cast<uint8_t*>(scratch);
-    const int64_t ntiles = N / MMA_TILE_ROWS, ngroups = K / 256, nblk = K / 32;
-    GemvArgs a;
-    a.W = static_cast<const uint8_t*>(W);
+    const int64_t ngroups = K / 256, nblk = K / 32;
     a.frags = base + L.frags;
     a.zeros = base + L.zeros;
     a.scale = reinterpret_cast<const float*>(base + L.scale);
     a.xsum = reinterpret_cast<const float*>(base + L.xsum);
-    a.y = y;
     a.count = reinterpret_cast<int*>(base + L.count);
     a.partial = reinterpret_cast<float*>(base + L.partial);
     a.ngroups = ngroups;
@@ -502,7 +542,7 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cudaLaunchConfig_t cp = {};
-    int64_t xblocks = (nblk + 1) / 2;                       // one warp per 32-value block
+    int64_t xblocks = (nblk + 1) / 2;                                // one warp per 32-value block
     if ((ntiles + 63) / 64 > xblocks) xblocks = (ntiles + 63) / 64;  // and a thread per tile counter
     if (xblocks > 4096) xblocks = 4096;
     cp.gridDim = dim3(static_cast<unsigned>(xblocks));
