@@ -174,22 +174,25 @@ struct GemvArgs {
     int64_t ngroups, units, nwarps;
 };
 
-// matrix of a (global) tile, and the tile's first byte / first output row
-__device__ __forceinline__ int seg_of(const GemvArgs& a, int64_t tile) {
-    int s = 0;
+// Matrix s of a (global) tile, and that matrix's first tile, weights and
+// output; constant-index selects keep the parameter arrays in the constant
+// bank (no dynamically indexed copy of the arguments).
+struct SegRef {
+    const uint8_t* W;
+    float* y;
+    int64_t first_tile, end_tile;
+};
+__device__ __forceinline__ SegRef seg_ref(const GemvArgs& a, int64_t tile) {
+    SegRef r{a.W[0], a.y[0], 0, a.tile_end[0]};
 #pragma unroll
-    for (int i = 0; i < kMaxSegs - 1; ++i) s += (i + 1 < a.nseg && tile >= a.tile_end[i]) ? 1 : 0;
-    return s;
-}
-__device__ __forceinline__ const uint8_t* tile_weights(const GemvArgs& a, int s, int64_t tile) {
-    return a.W[s] + (tile - (s ? a.tile_end[s - 1] : 0)) * a.ngroups * MMA_GROUP_BYTES;
-}
-__device__ __forceinline__ float* tile_out(const GemvArgs& a, int s, int64_t tile) {
-    return a.y[s] + (tile - (s ? a.tile_end[s - 1] : 0)) * MMA_TILE_ROWS;
+    for (int i = 1; i < kMaxSegs; ++i)
+        if (i < a.nseg && tile >= a.tile_end[i - 1]) r = SegRef{a.W[i], a.y[i], a.tile_end[i - 1], a.tile_end[i]};
+    return r;
 }
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
     const int64_t tile = u / a.ngroups;
-    return tile_weights(a, seg_of(a, tile), tile) + (u - tile * a.ngroups) * MMA_GROUP_BYTES;
+    const SegRef r = seg_ref(a, tile);
+    return r.W + ((tile - r.first_tile) * a.ngroups + (u - tile * a.ngroups)) * MMA_GROUP_BYTES;
 }
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
@@ -282,31 +285,37 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
 
 template <int TYPE>
 __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(const GemvArgs a) {
+    // unit, tile and group counts fit in 32 bits (the launcher checks)
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int64_t U = a.units, NW = a.nwarps, ng = a.ngroups;
-    const int64_t w = int64_t(blockIdx.x) * kWarps + (threadIdx.x >> 5);
-    const int64_t u0 = w < NW ? w * U / NW : 0, u1 = w < NW ? (w + 1) * U / NW : 0;
+    const int U = static_cast<int>(a.units), NW = static_cast<int>(a.nwarps), ng = static_cast<int>(a.ngroups);
+    const int w = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+    const int u0 = w < NW ? static_cast<int>(int64_t(w) * U / NW) : 0;
+    const int u1 = w < NW ? static_cast<int>(int64_t(w + 1) * U / NW) : 0;
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
-        for (int64_t d = 0; d < kPrefetch && u0 + d < u1; ++d) prefetch_l2(unit_weights(a, u0 + d), MMA_GROUP_BYTES);
+        for (int d = 0; d < kPrefetch && u0 + d < u1; ++d) prefetch_l2(unit_weights(a, u0 + d), MMA_GROUP_BYTES);
     pdl_release();
     pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel
 
     const bool supplier = g == t || g == t + 4;
     const uint8_t* fb0 = supplier ? a.frags + g * kSlotBytes : a.zeros;
     const int fc = supplier ? kChunkFragBytes : 0;
-    const int64_t fg = supplier ? kGroupFragBytes : 0;
-    int64_t u = u0;
+    const int fg = supplier ? kGroupFragBytes : 0;
+    int u = u0;
     while (u < u1) {
-        const int64_t tile = u / ng, tbeg = tile * ng;
-        const int64_t gend = (u1 - tbeg) < ng ? (u1 - tbeg) : ng;
-        const int seg = seg_of(a, tile);
-        const uint8_t* tw = tile_weights(a, seg, tile);
-        float* ty = tile_out(a, seg, tile);
+        const int tile = u / ng, tbeg = tile * ng;
+        const int gend = (u1 - tbeg) < ng ? (u1 - tbeg) : ng;
+        const uint8_t* tw;
+        int pf_end;  // a matrix's tiles are contiguous: prefetch ahead up to its last unit
+        {
+            const SegRef sr = seg_ref(a, tile);
+            tw = sr.W + static_cast<int64_t>(tile - static_cast<int>(sr.first_tile)) * ng * MMA_GROUP_BYTES;
+            pf_end = (static_cast<int>(sr.end_tile) - tile) * ng;
+        }
         float y0 = 0.f, y8 = 0.f;
-        for (int64_t gi = u - tbeg; gi < gend; ++gi) {
-            const int64_t ua = tbeg + gi;
-            if (lane == 0 && ua + kPrefetch < u1) prefetch_l2(unit_weights(a, ua + kPrefetch), MMA_GROUP_BYTES);
+        for (int gi = u - tbeg; gi < gend; ++gi) {
+            if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
+                prefetch_l2(tw + (gi + kPrefetch) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
             group_dot<TYPE>(tw + gi * MMA_GROUP_BYTES, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g, t,
                             y0, y8);
         }
@@ -314,6 +323,11 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
         y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
         y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+        float* ty;  // looked up again here so that nothing extra stays live in the loop above
+        {
+            const SegRef sr = seg_ref(a, tile);
+            ty = sr.y + (tile - static_cast<int>(sr.first_tile)) * MMA_TILE_ROWS;
+        }
         if (u == tbeg && gend == ng) {  // the whole tile is this warp's
             if (t == 0) {
                 ty[g] = y0;
@@ -330,19 +344,19 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             int prev = 0;
             if (lane == 0) prev = atomicAdd(a.count + tile, 1);
             prev = __shfl_sync(0xffffffffu, prev, 0);
-            const int64_t wa = warp_of(tbeg, U, NW), wb = warp_of(tbeg + ng - 1, U, NW);
-            if (prev == static_cast<int>(wb - wa)) {  // last contributor
+            const int wa = static_cast<int>(warp_of(tbeg, U, NW)), wb = static_cast<int>(warp_of(tbeg + ng - 1, U, NW));
+            if (prev == wb - wa) {  // last contributor
                 __threadfence();
                 // lane (row r, half h) adds contributors wa + h, wa + h + 2, ...
                 // in a fixed order, eight independent loads in flight at a time
                 const int r = lane & 15, h = lane >> 4;
-                const int slot_a = (wa * U / NW < tbeg) ? 1 : 0;  // wa's last tile, else its first
+                const int slot_a = (int64_t(wa) * U / NW < tbeg) ? 1 : 0;  // wa's last tile, else its first
                 float acc = 0.f;
-                for (int64_t v0 = wa + h; v0 <= wb; v0 += 16) {
+                for (int v0 = wa + h; v0 <= wb; v0 += 16) {
                     float part[8];
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        const int64_t v = v0 + 2 * j;
+                        const int v = v0 + 2 * j;
                         const int slot = v == wa ? slot_a : 0;
                         part[j] = v <= wb ? __ldcg(a.partial + (v * 2 + slot) * MMA_TILE_ROWS + r) : 0.f;
                     }
@@ -525,6 +539,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     a.partial = reinterpret_cast<float*>(base + L.partial);
     a.ngroups = ngroups;
     a.units = ntiles * ngroups;
+    if (a.units >= (int64_t(1) << 31)) return cudaErrorInvalidValue;  // the kernel counts units in 32 bits
 
     static int s_sms[16] = {};
     int dev = 0;
