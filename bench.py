@@ -157,6 +157,19 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def profiled_traffic() -> tuple[int | None, str]:
+    """DRAM bytes (read + write) of one step's GEMV launches, from the committed
+    ncu launch-list summary of this workload (profiles/decode70b_q4k_launches.md)."""
+    p = os.path.join(ROOT, "profiles", "decode70b_q4k_launches.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_step:"):
+                return int(line.split(":")[1].split()[0]), "profiles/decode70b_q4k_launches.md"
+    except (OSError, ValueError):
+        pass
+    return None, "no profile"
+
+
 def measured_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -433,6 +446,7 @@ def run_b200_arm(args, dist: Dist) -> None:
     # dominant kernel alone (local shards, no collectives)
     k_ms = dist.max(kernel_only_ms(torch, G, model, max(2, args.steps // 2)))
     peak, peak_src = measured_peak()
+    traffic, traffic_src = profiled_traffic() if dist.world == 1 else (None, "profiled at N=1 only")
     achieved = model.local_bytes / (k_ms * 1e-3) / 1e9
 
     cpu = None
@@ -464,7 +478,8 @@ def run_b200_arm(args, dist: Dist) -> None:
             "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<12> (Q4_K) with its xprep_kernel",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
-                         "traffic": None, "per_launch_note": f"{LAUNCHES_PER_TOKEN} GEMV launches per step (q/k/v and gate/up "
+                         "traffic": traffic, "traffic_unit": "bytes per step (all GEMV launches)",
+                         "traffic_source": traffic_src, "algorithmic_bytes_per_step": model.local_bytes, "per_launch_note": f"{LAUNCHES_PER_TOKEN} GEMV launches per step (q/k/v and gate/up "
                          "fused); achieved = local weight bytes per step / GEMV-only device time per step"},
             "clocks": clk.summary(),
             # per launch group (q/k/v and gate/up fused, o, down, lm_head):

@@ -3,7 +3,7 @@
 //
 // Reference counterparts:
 //   src/ggml-xdna.cpp:95-147    supports_op_impl      -> supports_mul_mat()
-//   src/ggml-xdna.cpp:149-308   process_mul_mat_node  -> plan_node()/run_jobs()
+//   src/ggml-xdna.cpp:149-308   process_mul_mat_node  -> run_node(), run_fused()
 //   src/ggml-xdna.cpp:316-470   buffer / buffer-type  -> Buffer, BufferType
 //   src/ggml-xdna.cpp:719-844   compat entry points   -> extern "C" section
 //   src/dma_streamer.cpp:153-419 bounded 2-slot pinned staging -> Staging
