@@ -1,0 +1,98 @@
+"""Row-sharded GEMV over two GPUs through the C ABI (NCCL all-gather).
+
+Each of two processes drives one GPU with ggml_backend_xdna_init_sharded,
+uploads its rows of every weight (ggml_backend_xdna_shard_rows) and runs one
+compute_graph call: two nodes that share x (fused into one launch per rank)
+and a third single node.  Both ranks must end with the full outputs, equal
+to the oracle.  Needs two GPUs; skipped otherwise.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _worker(rank: int, tmp: str, seed: int) -> None:
+    import ctypes as C
+    import sys
+    import time
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for sub in ("xdna.cpp_b200", "oracle", "tests"):
+        sys.path.insert(0, os.path.join(root, sub))
+    import torch
+
+    import ggml_b200 as G
+    import oracle as O
+    from helpers import normal_weights, normal_x
+
+    torch.cuda.set_device(rank)
+    idf = os.path.join(tmp, "nccl_id")
+    if rank == 0:
+        with open(idf + ".tmp", "wb") as f:
+            f.write(G.nccl_unique_id())
+        os.replace(idf + ".tmp", idf)
+    for _ in range(600):  # the id file appears within seconds
+        if os.path.exists(idf):
+            break
+        time.sleep(0.1)
+    nccl_id = open(idf, "rb").read()
+    K = 2048
+    mats = [(G.Q4_K, 1024), (G.Q4_K, 256), (G.Q4_0, 512)]  # two fused (same x), one single (Q4_0)
+    x = normal_x(K, seed + 1)
+    with G.Backend(rank, WORLD, rank, nccl_id) as be:
+        buf = G.Buffer(sum(N * G.row_bytes(t, K) for t, N in mats) // WORLD + 64 * 1024, dev=rank)
+        d_x = torch.from_numpy(x).cuda()
+        outs, nodes, refs, keep = [], [], [], []
+        for i, (t, N) in enumerate(mats):
+            raw = O.quantize(t, normal_weights(N, K, seed + 10 + i), nthreads=4)
+            refs.append(O.gemv(t, raw, N, K, x, nthreads=4))
+            r0, nr = C.c_int64(), C.c_int64()
+            G.check(G.lib().ggml_backend_xdna_shard_rows(N, WORLD, rank, C.byref(r0), C.byref(nr)), "shard_rows")
+            rb = G.row_bytes(t, K)
+            mine = np.ascontiguousarray(raw[r0.value * rb:(r0.value + nr.value) * rb])
+            w = buf.alloc(G.tensor(t, [K, nr.value, 1, 1]))
+            buf.set(w, mine.ctypes.data, 0, mine.nbytes)
+            y = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+            xt = G.tensor(G.F32, [K, 1, 1, 1], data=d_x.data_ptr())
+            nodes.append(G.mul_mat_node(w, xt, y.data_ptr(), N, name=f"m{i}"))
+            outs.append(y)
+            keep += [w, xt, mine]
+        ok = be.compute(nodes)
+        be.synchronize()
+        res = {"ok": ok, "err": G.last_error() if not ok else ""}
+        for i, y in enumerate(outs):
+            s = O.stats(y.cpu().numpy(), refs[i])
+            res[f"cos{i}"], res[f"rel{i}"] = s["cos"], s["maxabs_rel"]
+        buf.free()
+    np.save(os.path.join(tmp, f"res{rank}.npy"), np.array([res], dtype=object), allow_pickle=True)
+
+
+def test_row_sharded_nodes_over_two_gpus(cuda, tmp_path):
+    if cuda.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, str(tmp_path), 314)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    from helpers import COS_MIN, MAXABS_REL
+
+    for r in range(WORLD):
+        res = np.load(tmp_path / f"res{r}.npy", allow_pickle=True)[0]
+        assert res["ok"], res
+        for i in range(3):
+            assert res[f"cos{i}"] >= COS_MIN and res[f"rel{i}"] <= MAXABS_REL, (r, i, res)

@@ -600,13 +600,19 @@ double nccl_timeout_s() {
 bool nccl_wait(ncclComm_t comm, ncclResult_t r, const char* what) {
     const NcclApi& api = nccl_api();
     const auto t0 = std::chrono::steady_clock::now();
+    // enqueueing a collective on a non-blocking communicator finishes within
+    // microseconds: spin (yielding) first, sleep only if it takes longer
     while (r == ncclInProgress) {
-        if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > nccl_timeout_s()) {
+        const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (el > nccl_timeout_s()) {
             api.CommAbort(comm);
             set_error("%s: timed out after %.0f s (communicator aborted)", what, nccl_timeout_s());
             return false;
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        if (el < 2e-3)
+            std::this_thread::yield();
+        else
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
         if (api.CommGetAsyncError(comm, &r) != ncclSuccess) break;
     }
     if (r != ncclSuccess) {
@@ -856,9 +862,19 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n) {
     if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true),
                  "fused gemv launch"))
         return false;
-    for (size_t k = 0; k < n; ++k)
-        if (f[k].sharded && !all_gather_rows(be, f[k].y_full, f[k].seg.N)) return false;
-    return true;
+    bool any = false;
+    for (size_t k = 0; k < n; ++k) any = any || f[k].sharded;
+    if (!any) return true;
+    // one NCCL group: the slices of every fused node travel in one launch
+    const NcclApi& api = nccl_api();
+    ncclResult_t r = api.GroupStart();
+    for (size_t k = 0; k < n && r == ncclSuccess; ++k)
+        if (f[k].sharded)
+            r = api.AllGather(f[k].y_full + be->rank * f[k].seg.N, f[k].y_full, static_cast<size_t>(f[k].seg.N),
+                              ncclFloat32, be->comm, be->stream);
+    const ncclResult_t e = api.GroupEnd();
+    if (r == ncclSuccess || r == ncclInProgress) r = e;
+    return nccl_wait(be->comm, r, "grouped ncclAllGather");
 }
 
 }  // namespace
