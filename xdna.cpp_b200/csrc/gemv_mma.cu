@@ -66,10 +66,17 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 // equal-sized range of units (warp w: [w U / NW, (w + 1) U / NW)), so every
 // warp streams the same number of bytes whatever N and K are: no partial
 // waves, no idle SMs on short matrices.  A tile whose groups are split across
-// warps is finished by the warp that arrives last at the tile's counter: it
-// adds the contributors' partial rows in warp order (deterministic) and
-// writes y.  A warp has at most two split tiles (its first and its last), so
-// its partials need two 16-float slots.
+// warps is combined in two levels, always adding in a fixed order
+// (deterministic results):
+//   1. each contributor writes its 16 partial rows to shared memory (two
+//      slots per warp: a warp can share only its first and its last tile) and
+//      counts itself in with a shared-memory atomic; the CTA's last
+//      contributor adds the CTA's partials in warp order;
+//   2. if the tile also has contributors in other CTAs (only a CTA's first
+//      and last tile can), that warp writes the CTA's sum to global memory
+//      and counts in at the tile's global counter; the last CTA adds the
+//      CTAs' sums in CTA order.  Otherwise it writes y directly.
+// Only tiles that cross a CTA boundary pay for a device-scope fence and atomic.
 //
 // Scratch of one launch (all offsets 256-byte aligned):
 //   frags   per group, per chunk c (32 values of each of the 8 blocks), per
@@ -80,7 +87,7 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //   zeros   32 zero bytes: the B "slot" of the 24 lanes that supply nothing
 //   scale   2^e per 32-value block;  xsum  sum of the block's x
 //   count   one arrival counter per tile (zeroed by xprep_kernel)
-//   partial kMaxCtas * 8 warps * 2 slots * 16 floats
+//   partial kMaxCtas CTAs * 2 slots * 16 floats (level-2 CTA sums)
 // ---------------------------------------------------------------------------
 constexpr int kWarps = 8;
 constexpr int kGemvThreads = kWarps * 32;
@@ -172,6 +179,7 @@ struct GemvArgs {
     int* count;
     float* partial;
     int64_t ngroups, units, nwarps;
+    int cta_tiles;  // bound on the tiles one CTA's units touch (shared-memory counters)
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -291,6 +299,13 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     const int w = static_cast<int>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
     const int u0 = w < NW ? static_cast<int>(int64_t(w) * U / NW) : 0;
     const int u1 = w < NW ? static_cast<int>(int64_t(w + 1) * U / NW) : 0;
+    // shared memory: per-warp partial rows (2 slots) and one arrival counter
+    // per tile this CTA touches, counted from t0, the tile of its first unit
+    extern __shared__ __align__(16) float s_part[];
+    int* s_count = reinterpret_cast<int*>(s_part + kWarps * 2 * MMA_TILE_ROWS);
+    const int t0 = static_cast<int>(int64_t(blockIdx.x) * kWarps * U / NW) / ng;
+    for (int i = threadIdx.x; i < a.cta_tiles; i += blockDim.x) s_count[i] = 0;
+    __syncthreads();
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
         for (int d = 0; d < kPrefetch && u0 + d < u1; ++d) prefetch_l2(unit_weights(a, u0 + d), MMA_GROUP_BYTES);
@@ -334,37 +349,62 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                 ty[g + 8] = y8;
             }
         } else {
-            float* mine = a.partial + (w * 2 + (u == u0 ? 0 : 1)) * MMA_TILE_ROWS;
+            // the tile's contributors are global warps wa..wb; this CTA holds lo..hi of them
+            const int wa = static_cast<int>(warp_of(tbeg, U, NW)), wb = static_cast<int>(warp_of(tbeg + ng - 1, U, NW));
+            const int cta = static_cast<int>(blockIdx.x);
+            const int lo = wa > cta * kWarps ? wa : cta * kWarps;
+            const int hi = wb < cta * kWarps + kWarps - 1 ? wb : cta * kWarps + kWarps - 1;
+            const int slot_a = (int64_t(wa) * U / NW < tbeg) ? 1 : 0;  // wa's last tile, else its first
+            // level 1: partial rows to shared memory; the CTA's last contributor adds them
+            float* mine = s_part + ((w - cta * kWarps) * 2 + (u == u0 ? 0 : 1)) * MMA_TILE_ROWS;
             if (t == 0) {
                 mine[g] = y0;
                 mine[g + 8] = y8;
             }
-            __threadfence();
+            __threadfence_block();
             __syncwarp();
             int prev = 0;
-            if (lane == 0) prev = atomicAdd(a.count + tile, 1);
+            if (lane == 0) prev = atomicAdd(s_count + (tile - t0), 1);
             prev = __shfl_sync(0xffffffffu, prev, 0);
-            const int wa = static_cast<int>(warp_of(tbeg, U, NW)), wb = static_cast<int>(warp_of(tbeg + ng - 1, U, NW));
-            if (prev == wb - wa) {  // last contributor
-                __threadfence();
-                // lane (row r, half h) adds contributors wa + h, wa + h + 2, ...
-                // in a fixed order, eight independent loads in flight at a time
-                const int r = lane & 15, h = lane >> 4;
-                const int slot_a = (int64_t(wa) * U / NW < tbeg) ? 1 : 0;  // wa's last tile, else its first
+            if (prev == hi - lo) {
+                __threadfence_block();
+                const int r = lane & 15;
                 float acc = 0.f;
-                for (int v0 = wa + h; v0 <= wb; v0 += 16) {
-                    float part[8];
+                for (int v = lo; v <= hi; ++v)  // warp order
+                    acc += s_part[((v - cta * kWarps) * 2 + (v == wa ? slot_a : 0)) * MMA_TILE_ROWS + r];
+                const int ca = wa / kWarps, cb = wb / kWarps;
+                if (ca == cb) {  // every contributor was in this CTA
+                    if (lane < MMA_TILE_ROWS) ty[r] = acc;
+                } else {
+                    // level 2: the CTA's sum to global memory; the last CTA adds them in CTA order.
+                    // A CTA shares at most two tiles with others: its first (slot 0) and last (slot 1).
+                    if (lane < MMA_TILE_ROWS) a.partial[(cta * 2 + (tile == t0 ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
+                    __threadfence();
+                    __syncwarp();
+                    int gprev = 0;
+                    if (lane == 0) gprev = atomicAdd(a.count + tile, 1);
+                    gprev = __shfl_sync(0xffffffffu, gprev, 0);
+                    if (gprev == cb - ca) {
+                        __threadfence();
+                        // lane (row r, half h) adds CTAs ca + h, ca + h + 2, ..., eight loads in flight
+                        const int h = lane >> 4;
+                        const int t0a = static_cast<int>(int64_t(ca * kWarps) * U / NW) / ng;  // CTA ca's first tile
+                        float sum = 0.f;
+                        for (int c0 = ca + h; c0 <= cb; c0 += 16) {
+                            float part[8];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int v = v0 + 2 * j;
-                        const int slot = v == wa ? slot_a : 0;
-                        part[j] = v <= wb ? __ldcg(a.partial + (v * 2 + slot) * MMA_TILE_ROWS + r) : 0.f;
+                            for (int j = 0; j < 8; ++j) {
+                                const int c = c0 + 2 * j;
+                                const int which = (c == ca && t0a != tile) ? 1 : 0;
+                                part[j] = c <= cb ? __ldcg(a.partial + (c * 2 + which) * MMA_TILE_ROWS + r) : 0.f;
+                            }
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) sum += part[j];
+                        }
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+                        if (h == 0) ty[r] = sum;
                     }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc += part[j];
                 }
-                acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-                if (h == 0) ty[r] = acc;
             }
         }
         u = tbeg + gend;
@@ -489,7 +529,7 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
     L.xsum = up(L.scale + nblk * sizeof(float));
     L.count = up(L.xsum + nblk * sizeof(float));
     L.partial = up(L.count + ntiles * sizeof(int));
-    L.total = up(L.partial + size_t(kMaxCtas) * kWarps * 2 * MMA_TILE_ROWS * sizeof(float));
+    L.total = up(L.partial + size_t(kMaxCtas) * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
 }
 
@@ -552,6 +592,12 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     if (blocks > (a.units + kWarps - 1) / kWarps) blocks = (a.units + kWarps - 1) / kWarps;
     if (blocks < 1) blocks = 1;
     a.nwarps = blocks * kWarps < a.units ? blocks * kWarps : a.units;
+    {
+        const int64_t per_warp = (a.units + a.nwarps - 1) / a.nwarps;
+        a.cta_tiles = static_cast<int>((kWarps * per_warp + ngroups - 1) / ngroups + 2);
+    }
+    const size_t smem = size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(a.cta_tiles) * sizeof(int);
+    if (smem > 48 * 1024) return cudaErrorInvalidValue;  // beyond any shape the layout admits
 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -573,6 +619,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks));
     cg.blockDim = dim3(kGemvThreads);
+    cg.dynamicSmemBytes = smem;
     cg.stream = stream;
     cudaLaunchAttribute attr2[1];
     attr2[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -586,7 +633,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
 // Fixed scratch of b200_gemv_noalloc: one static device array per device
 // instead of buffers allocated on demand.  1 MiB holds the layout above for
 // N <= 131072 rows with K <= 32768 (frags 256 KiB, counters 32 KiB, partial
-// slots 512 KiB, scales and sums 8 KiB).  Nothing in it has to start zeroed:
+// slots 64 KiB, scales and sums 8 KiB).  Nothing in it has to start zeroed:
 // every launch's xprep_kernel writes the digits and clears the tile counters
 // before the GEMV reads them.  It is shared by every stream of the device.
 static __device__ __align__(256) unsigned char g_static_scratch[size_t(1) << 20];
