@@ -1,10 +1,16 @@
-"""Row-sharded GEMV over two GPUs through the C ABI (NCCL all-gather).
+"""Row-sharded GEMV over two GPUs through the C ABI.
 
 Each of two processes drives one GPU with ggml_backend_xdna_init_sharded,
 uploads its rows of every weight (ggml_backend_xdna_shard_rows) and runs one
 compute_graph call: two nodes that share x (fused into one launch per rank)
 and a third single node.  Both ranks must end with the full outputs, equal
-to the oracle.  Needs two GPUs; skipped otherwise.
+to the oracle, over the peer exchange (rows stored into the peers' buffers
+by the GEMV) and over the NCCL all-gather fallback.
+
+Failure detection: a rank that skips a step must not hang the other; the
+other's bounded wait ends and compute_graph reports the missing rows.
+
+Needs two GPUs; skipped otherwise.  NVLS stays off (NCCL_NVLS_ENABLE=0).
 """
 from __future__ import annotations
 
@@ -18,7 +24,7 @@ pytestmark = pytest.mark.gpu
 WORLD = 2
 
 
-def _worker(rank: int, tmp: str, seed: int) -> None:
+def _worker(rank: int, tmp: str, seed: int, mode: str = "run") -> None:
     import ctypes as C
     import sys
     import time
@@ -32,6 +38,9 @@ def _worker(rank: int, tmp: str, seed: int) -> None:
     import oracle as O
     from helpers import normal_weights, normal_x
 
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if mode == "nccl":
+        os.environ["XDNA_B200_NO_P2P"] = "1"
     torch.cuda.set_device(rank)
     idf = os.path.join(tmp, "nccl_id")
     if rank == 0:
@@ -64,9 +73,24 @@ def _worker(rank: int, tmp: str, seed: int) -> None:
             nodes.append(G.mul_mat_node(w, xt, y.data_ptr(), N, name=f"m{i}"))
             outs.append(y)
             keep += [w, xt, mine]
-        ok = be.compute(nodes)
+        done = os.path.join(tmp, "rank0_done")
+        if mode == "skip" and rank == 1:
+            # this rank leaves the step before it starts, but keeps its memory
+            # (which rank 0's kernels still write to) until rank 0 is through
+            ok, t_call = True, 0.0
+            for _ in range(600):
+                if os.path.exists(done):
+                    break
+                time.sleep(0.1)
+        else:
+            t = time.perf_counter()
+            ok = be.compute(nodes)
+            t_call = time.perf_counter() - t
+            be.synchronize()
+            if rank == 0:
+                open(done, "w").close()
         be.synchronize()
-        res = {"ok": ok, "err": G.last_error() if not ok else ""}
+        res = {"ok": ok, "err": G.last_error() if not ok else "", "t_call": t_call}
         for i, y in enumerate(outs):
             s = O.stats(y.cpu().numpy(), refs[i])
             res[f"cos{i}"], res[f"rel{i}"] = s["cos"], s["maxabs_rel"]
@@ -74,13 +98,11 @@ def _worker(rank: int, tmp: str, seed: int) -> None:
     np.save(os.path.join(tmp, f"res{rank}.npy"), np.array([res], dtype=object), allow_pickle=True)
 
 
-def test_row_sharded_nodes_over_two_gpus(cuda, tmp_path):
-    if cuda.cuda.device_count() < WORLD:
-        pytest.skip("needs two GPUs")
+def _run(tmp_path, mode):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, str(tmp_path), 314)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, str(tmp_path), 314, mode)) for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
@@ -89,10 +111,24 @@ def test_row_sharded_nodes_over_two_gpus(cuda, tmp_path):
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    return [np.load(tmp_path / f"res{r}.npy", allow_pickle=True)[0] for r in range(WORLD)]
+
+
+@pytest.mark.parametrize("mode", ["run", "nccl"])
+def test_row_sharded_nodes_over_two_gpus(cuda, tmp_path, mode):
+    if cuda.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
     from helpers import COS_MIN, MAXABS_REL
 
-    for r in range(WORLD):
-        res = np.load(tmp_path / f"res{r}.npy", allow_pickle=True)[0]
+    for r, res in enumerate(_run(tmp_path, mode)):
         assert res["ok"], res
         for i in range(3):
             assert res[f"cos{i}"] >= COS_MIN and res[f"rel{i}"] <= MAXABS_REL, (r, i, res)
+
+
+def test_rank_missing_a_step_is_reported_not_hung(cuda, tmp_path):
+    if cuda.cuda.device_count() < WORLD:
+        pytest.skip("needs two GPUs")
+    res = _run(tmp_path, "skip")
+    assert not res[0]["ok"] and "did not arrive" in res[0]["err"], res[0]
+    assert res[0]["t_call"] < 30.0, res[0]

@@ -301,6 +301,17 @@ struct Backend {
     void* xscratch[2] = {nullptr, nullptr};
     size_t xscratch_bytes = 0;
     int xscratch_next = 0;
+    // Peer exchange of row-sharded MMA launches (see setup_exchange): this
+    // rank's region (flag words, then two data halves used by alternate
+    // launches) and every rank's region mapped into this process.
+    struct Exchange {
+        bool ok = false;
+        char* local = nullptr;
+        char* peer[kMaxPeers] = {};
+        size_t cap_floats = 0;  // floats per data half
+        uint32_t epoch = 0;
+        int* err = nullptr;     // set by a gather kernel whose wait timed out
+    } xg;
 };
 
 // A scratch slot of at least xprep_bytes(N, K); growing it drains the stream first.
@@ -325,6 +336,89 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
     void* p = be->xscratch[be->xscratch_next];
     be->xscratch_next ^= 1;
     return p;
+}
+
+bool nccl_wait(ncclComm_t comm, ncclResult_t r, const char* what);
+
+// Exchange regions: [flags: one uint32 per source rank, 256 B][half 0][half 1].
+constexpr size_t kXchgFlagBytes = 256;
+
+void release_exchange(Backend* be) {
+    Backend::Exchange& x = be->xg;
+    for (int p = 0; p < kMaxPeers; ++p)
+        if (x.peer[p] && x.peer[p] != x.local) cudaIpcCloseMemHandle(x.peer[p]);
+    if (x.local) cudaFree(x.local);
+    if (x.err) cudaFree(x.err);
+    x = Backend::Exchange{};
+}
+
+// Allocate this rank's exchange region, swap IPC handles with the other ranks
+// over NCCL and map theirs.  Any failure leaves the backend on the NCCL
+// all-gather path (x.ok stays false) with the reason in the error string.
+bool setup_exchange(Backend* be) {
+    Backend::Exchange& x = be->xg;
+    if (be->world < 2 || be->world > kMaxPeers || getenv("XDNA_B200_NO_P2P")) return false;
+    const char* mb = getenv("XDNA_B200_XCHG_MB");
+    const size_t half_bytes = (mb ? static_cast<size_t>(atol(mb)) : 16) << 20;
+    x.cap_floats = half_bytes / sizeof(float);
+    const size_t bytes = kXchgFlagBytes + 2 * half_bytes;
+    bool ok = cuda_ok(cudaMalloc(&x.local, bytes), "exchange alloc") &&
+              cuda_ok(cudaMemset(x.local, 0, bytes), "exchange clear") &&
+              cuda_ok(cudaMalloc(&x.err, sizeof(int)), "exchange error word") &&
+              cuda_ok(cudaMemset(x.err, 0, sizeof(int)), "exchange error clear") &&
+              cuda_ok(cudaDeviceSynchronize(), "exchange clear sync");
+    cudaIpcMemHandle_t mine;
+    ok = ok && cuda_ok(cudaIpcGetMemHandle(&mine, x.local), "cudaIpcGetMemHandle");
+    // every rank must take part in the handle all-gather even if its own setup
+    // failed (a zero handle then tells the others to stay on NCCL)
+    if (!ok) memset(&mine, 0, sizeof mine);
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    char* d = nullptr;
+    std::vector<char> all(hb * be->world);
+    bool gathered = cuda_ok(cudaMalloc(&d, hb * be->world), "handle buffer");
+    if (gathered) {
+        gathered = cuda_ok(cudaMemcpy(d + hb * be->rank, &mine, hb, cudaMemcpyHostToDevice), "handle upload");
+        const NcclApi& api = nccl_api();
+        const ncclResult_t r = api.AllGather(d + hb * be->rank, d, hb, ncclInt8, be->comm, be->stream);
+        gathered = nccl_wait(be->comm, r, "handle all-gather") && gathered &&
+                   cuda_ok(cudaStreamSynchronize(be->stream), "handle sync") &&
+                   cuda_ok(cudaMemcpy(all.data(), d, hb * be->world, cudaMemcpyDeviceToHost), "handle download");
+        cudaFree(d);
+    }
+    ok = ok && gathered;
+    static const char zero[sizeof(cudaIpcMemHandle_t)] = {};
+    for (int p = 0; p < be->world && ok; ++p) {
+        if (p == be->rank) {
+            x.peer[p] = x.local;
+            continue;
+        }
+        if (!memcmp(all.data() + hb * p, zero, hb)) {
+            ok = false;
+            break;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, all.data() + hb * p, hb);
+        void* ptr = nullptr;
+        ok = cuda_ok(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        x.peer[p] = static_cast<char*>(ptr);
+    }
+    if (!ok) {
+        cudaGetLastError();
+        release_exchange(be);
+        return false;
+    }
+    x.ok = true;
+    return true;
+}
+
+// A timed-out gather wait leaves its mark in the exchange's error word.
+bool exchange_error(Backend* be) {
+    if (!be->xg.ok) return false;
+    int e = 0;
+    if (cudaMemcpy(&e, be->xg.err, sizeof e, cudaMemcpyDeviceToHost) != cudaSuccess) return true;
+    if (!e) return false;
+    cudaMemset(be->xg.err, 0, sizeof(int));
+    return true;
 }
 
 Backend* as_backend(void* p) {
@@ -499,6 +593,12 @@ bool ranges_overlap(const void* a, size_t an, const void* b, size_t bn) {
 
 bool flush(Backend* be) {
     if (!cuda_ok(cudaStreamSynchronize(be->stream), "compute sync")) {
+        be->pending.clear();
+        be->dev_arena.used = be->host_arena.used = be->wt_arena.used = 0;
+        return false;
+    }
+    if (exchange_error(be)) {
+        set_error("row-sharded exchange: a peer's rows did not arrive within the wait limit");
         be->pending.clear();
         be->dev_arena.used = be->host_arena.used = be->wt_arena.used = 0;
         return false;
@@ -859,6 +959,40 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n) {
     }
     void* scratch = backend_xscratch(be, rows, f[0].K);
     if (!scratch) return false;
+    // row-sharded: rows travel to the peers from the GEMV itself when the
+    // outputs fit the exchange buffers; NCCL all-gather otherwise
+    int64_t full = 0;
+    bool all_sharded = true;
+    for (size_t k = 0; k < n; ++k) {
+        full += f[k].n_out;
+        all_sharded = all_sharded && f[k].sharded;
+    }
+    if (be->xg.ok && all_sharded && static_cast<size_t>(full) <= be->xg.cap_floats) {
+        Backend::Exchange& xg = be->xg;
+        PeerExchange pe = {};
+        pe.world = be->world;
+        pe.rank = be->rank;
+        pe.epoch = ++xg.epoch;
+        const size_t half = kXchgFlagBytes + (pe.epoch & 1u) * xg.cap_floats * sizeof(float);
+        for (int p = 0; p < be->world; ++p) {
+            pe.peer_data[p] = reinterpret_cast<float*>(xg.peer[p] + half);
+            pe.peer_flags[p] = reinterpret_cast<uint32_t*>(xg.peer[p]);
+        }
+        GatherSeg gs[MMA_MAX_SEGMENTS];
+        int64_t off = 0;
+        for (size_t k = 0; k < n; ++k) {
+            pe.xo[k] = off;
+            gs[k] = GatherSeg{f[k].y_full, f[k].seg.N, off};
+            off += f[k].n_out;
+        }
+        return cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream,
+                                             true, &pe),
+                       "sharded gemv launch") &&
+               cuda_ok(xchg_gather_launch(reinterpret_cast<const float*>(xg.local + half),
+                                          reinterpret_cast<const uint32_t*>(xg.local), pe.epoch, be->world, be->rank,
+                                          gs, static_cast<int>(n), xg.err, be->stream),
+                       "exchange gather launch");
+    }
     if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true),
                  "fused gemv launch"))
         return false;
@@ -962,6 +1096,7 @@ ggml_backend_t ggml_backend_xdna_init_sharded(size_t dev_num, int world, int ran
         ggml_backend_xdna_free(be);
         return nullptr;
     }
+    setup_exchange(be);  // on failure the sharded nodes use NCCL all-gathers
     return be;
 }
 
@@ -989,6 +1124,7 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         be->wt_arena.release();
         for (void* p : be->xscratch)
             if (p) cudaFree(p);
+        release_exchange(be);
         if (be->comm) nccl_api().CommDestroy(be->comm);
         cudaStreamDestroy(be->stream);
         be->magic = 0;
@@ -1037,7 +1173,8 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
         FusableNode f[MMA_MAX_SEGMENTS];
         const size_t run = no_fuse ? 0 : fused_run_length(be, nodes, i, n_nodes, f);
         const size_t count = run > 1 ? run : 1;
-        ok = run > 1 ? run_fused(be, f, run) : run_node(be, node);
+        const bool fused = run > 1 || (run == 1 && f[0].sharded && be->xg.ok);
+        ok = fused ? run_fused(be, f, run) : run_node(be, node);
         for (size_t k = i; trace && ok && k < i + count; ++k)
             fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued%s\n", k,
                     nodes[k]->name[0] ? nodes[k]->name : "unnamed", nodes[k]->src[0]->type,

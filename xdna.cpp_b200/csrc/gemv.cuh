@@ -34,8 +34,31 @@ struct MmaSegment {
     float* y;
     int64_t N;
 };
+// Row-sharded launches (one process per GPU): besides writing its own rows of
+// y, the GEMV stores them into every peer's exchange buffer (peer memory
+// mapped over NVLink) and, when all its CTAs are done, raises its flag
+// (= epoch) in every peer's flag array.  A gather kernel on each GPU then
+// waits for the peers' flags and copies their rows into the full outputs.
+constexpr int kMaxPeers = 8;
+struct PeerExchange {
+    float* peer_data[kMaxPeers];       // each rank's exchange buffer for this launch
+    uint32_t* peer_flags[kMaxPeers];   // each rank's flag array (one word per source rank)
+    int world, rank;
+    uint32_t epoch;
+    int64_t xo[4];                     // segment s's first float in the exchange buffer
+};
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
-                                  void* scratch, cudaStream_t stream, bool pdl);
+                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr);
+// Copy the peers' rows of each segment from this GPU's exchange buffer into
+// the full outputs once every peer's flag reaches `epoch` (a bounded wait:
+// on time-out it sets *err and copies nothing).
+struct GatherSeg {
+    float* y_full;
+    int64_t n_local;
+    int64_t xo;
+};
+cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32_t epoch, int world, int rank,
+                               const GatherSeg* segs, int nseg, int* err, cudaStream_t stream);
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,
                               cudaStream_t stream);
 

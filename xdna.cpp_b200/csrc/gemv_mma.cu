@@ -180,6 +180,9 @@ struct GemvArgs {
     float* partial;
     int64_t ngroups, units, nwarps;
     int cta_tiles;  // bound on the tiles one CTA's units touch (shared-memory counters)
+    bool xchg;      // row-sharded launch: also store rows into the peers' exchange buffers
+    PeerExchange x;
+    int* done;      // CTAs finished (zeroed by xprep_kernel), for the completion flags
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -188,14 +191,38 @@ struct GemvArgs {
 struct SegRef {
     const uint8_t* W;
     float* y;
-    int64_t first_tile, end_tile;
+    int64_t first_tile, end_tile, xo;
 };
 __device__ __forceinline__ SegRef seg_ref(const GemvArgs& a, int64_t tile) {
-    SegRef r{a.W[0], a.y[0], 0, a.tile_end[0]};
+    SegRef r{a.W[0], a.y[0], 0, a.tile_end[0], a.x.xo[0]};
 #pragma unroll
     for (int i = 1; i < kMaxSegs; ++i)
-        if (i < a.nseg && tile >= a.tile_end[i - 1]) r = SegRef{a.W[i], a.y[i], a.tile_end[i - 1], a.tile_end[i]};
+        if (i < a.nseg && tile >= a.tile_end[i - 1])
+            r = SegRef{a.W[i], a.y[i], a.tile_end[i - 1], a.tile_end[i], a.x.xo[i]};
     return r;
+}
+
+// Output row `row` (0..15) of global tile `tile`: to y, and for a sharded
+// launch to the same place of every peer's exchange buffer (NVLink stores).
+__device__ __forceinline__ void emit(const GemvArgs& a, float* ty, int tile, int row, float v) {
+    ty[row] = v;
+    if (a.xchg) {
+        const SegRef sr = seg_ref(a, tile);
+        const int64_t n_local = (sr.end_tile - sr.first_tile) * MMA_TILE_ROWS;
+        const int64_t off = sr.xo + a.x.rank * n_local + (tile - sr.first_tile) * MMA_TILE_ROWS + row;
+#pragma unroll
+        for (int p = 0; p < kMaxPeers; ++p)
+            if (p < a.x.world && p != a.x.rank) a.x.peer_data[p][off] = v;
+    }
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
     const int64_t tile = u / a.ngroups;
@@ -345,8 +372,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         }
         if (u == tbeg && gend == ng) {  // the whole tile is this warp's
             if (t == 0) {
-                ty[g] = y0;
-                ty[g + 8] = y8;
+                emit(a, ty, tile, g, y0);
+                emit(a, ty, tile, g + 8, y8);
             }
         } else {
             // the tile's contributors are global warps wa..wb; this CTA holds lo..hi of them
@@ -374,7 +401,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     acc += s_part[((v - cta * kWarps) * 2 + (v == wa ? slot_a : 0)) * MMA_TILE_ROWS + r];
                 const int ca = wa / kWarps, cb = wb / kWarps;
                 if (ca == cb) {  // every contributor was in this CTA
-                    if (lane < MMA_TILE_ROWS) ty[r] = acc;
+                    if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc);
                 } else {
                     // level 2: the CTA's sum to global memory; the last CTA adds them in CTA order.
                     // A CTA shares at most two tiles with others: its first (slot 0) and last (slot 1).
@@ -402,12 +429,81 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                             for (int j = 0; j < 8; ++j) sum += part[j];
                         }
                         sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-                        if (h == 0) ty[r] = sum;
+                        if (h == 0) emit(a, ty, tile, r, sum);
                     }
                 }
             }
         }
         u = tbeg + gend;
+    }
+    if (a.xchg) {
+        // Every row this CTA stored (locally and into the peers' buffers) is
+        // ordered before its count-in at device scope; the last CTA to count
+        // in then fences at system scope, which, being cumulative over what it
+        // observed through the counter, orders all CTAs' stores before this
+        // rank's flag in each peer's flag array.  (A system-scope fence in
+        // every CTA cost about 8 us per launch.)
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
+                __threadfence_system();
+                for (int p = 0; p < a.x.world; ++p)
+                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, a.x.epoch);
+            }
+        }
+    }
+}
+
+// Peers' rows -> the full outputs, after every peer's flag reached `epoch`.
+// Launched with programmatic dependent launch: it waits on the peers' flags
+// while this GPU's GEMV drains, then (griddepcontrol.wait) on that GEMV before
+// finishing, so the next kernel sees both halves of every output.  The flag
+// wait is bounded (1 s of %globaltimer); on time-out *err is set and nothing
+// is copied, so the host reports an error instead of the GPU hanging.
+constexpr uint64_t kGatherWaitNs = 1000000000ull;  // 1 s of %globaltimer
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+struct GatherArgs {
+    GatherSeg seg[kMaxSegs];
+    int nseg;
+};
+__global__ void __launch_bounds__(256) xchg_gather_kernel(const float* __restrict__ xdata, const uint32_t* flags,
+                                                          uint32_t epoch, int world, int rank, const GatherArgs g,
+                                                          int* err) {
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = global_ns();
+        for (int p = 0; p < world && ok; ++p) {
+            if (p == rank) continue;
+            while (static_cast<int32_t>(ld_acquire_sys(flags + p) - epoch) < 0) {
+                if (global_ns() - t0 > kGatherWaitNs) {
+                    ok = 0;
+                    atomicExch(err, 1);
+                    break;
+                }
+                __nanosleep(32);
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    pdl_wait();  // this GPU's GEMV has finished (its own rows are in y)
+    if (!s_ok) return;
+    const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    for (int s = 0; s < g.nseg; ++s) {
+        const GatherSeg sg = g.seg[s];
+        for (int p = 0; p < world; ++p) {
+            if (p == rank) continue;  // own rows: written by the GEMV
+            float* dst = sg.y_full + p * sg.n_local;
+            const float* src = xdata + sg.xo + p * sg.n_local;
+            for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < sg.n_local; i += stride)
+                dst[i] = __ldcg(src + i);
+        }
     }
 }
 
@@ -528,7 +624,7 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
     L.scale = up(L.zeros + kSlotBytes);
     L.xsum = up(L.scale + nblk * sizeof(float));
     L.count = up(L.xsum + nblk * sizeof(float));
-    L.partial = up(L.count + ntiles * sizeof(int));
+    L.partial = up(L.count + (ntiles + 1) * sizeof(int));  // + the CTA completion counter
     L.total = up(L.partial + size_t(kMaxCtas) * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
 }
@@ -556,9 +652,15 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 }
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
-                                  void* scratch, cudaStream_t stream, bool pdl) {
+                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
     if ((type != T_Q4_K && type != T_Q4_0) || nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+    if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
+        return cudaErrorInvalidValue;
     GemvArgs a = {};
+    if (xchg) {
+        a.xchg = true;
+        a.x = *xchg;
+    }
     int64_t ntiles = 0;
     for (int s = 0; s < nseg; ++s) {
         if (layout_kind(type, segs[s].N, K) != 1) return cudaErrorInvalidValue;
@@ -576,6 +678,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     a.scale = reinterpret_cast<const float*>(base + L.scale);
     a.xsum = reinterpret_cast<const float*>(base + L.xsum);
     a.count = reinterpret_cast<int*>(base + L.count);
+    a.done = a.count + ntiles;
     a.partial = reinterpret_cast<float*>(base + L.partial);
     a.ngroups = ngroups;
     a.units = ntiles * ngroups;
@@ -613,7 +716,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cp.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, base + L.frags, base + L.zeros,
                                        reinterpret_cast<float*>(base + L.scale),
-                                       reinterpret_cast<float*>(base + L.xsum), a.count, ntiles);
+                                       reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1);
     if (e != cudaSuccess) return e;
 
     cudaLaunchConfig_t cg = {};
@@ -628,6 +731,31 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cg.numAttrs = 1;
     if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
+}
+
+cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32_t epoch, int world, int rank,
+                               const GatherSeg* segs, int nseg, int* err, cudaStream_t stream) {
+    if (nseg < 1 || nseg > kMaxSegs || world < 2 || world > kMaxPeers) return cudaErrorInvalidValue;
+    GatherArgs g = {};
+    int64_t total = 0;
+    for (int s = 0; s < nseg; ++s) {
+        g.seg[s] = segs[s];
+        total += segs[s].n_local * world;
+    }
+    g.nseg = nseg;
+    int64_t blocks = (total + 2047) / 2048;  // few CTAs poll the flags; each copies 8 floats per thread
+    if (blocks > 32) blocks = 32;
+    if (blocks < 1) blocks = 1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3(static_cast<unsigned>(blocks));
+    c.blockDim = dim3(256);
+    c.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    return cudaLaunchKernelEx(&c, xchg_gather_kernel, xdata, flags, epoch, world, rank, g, err);
 }
 
 // Fixed scratch of b200_gemv_noalloc: one static device array per device
