@@ -34,7 +34,7 @@ namespace xb {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kItemRows = 4;  // rows per warp work item (x reuse factor)
+constexpr int kItemRows = 2;  // rows per warp work item (x reuse factor)
 static_assert(TILE_ROWS % kItemRows == 0, "items must not straddle tiles");
 constexpr int kWarps = kThreads / 32;
 constexpr float kMagic = 8388608.0f;  // 2^23
@@ -601,7 +601,7 @@ size_t smem_bytes(int64_t K) {
 }
 
 template <class D>
-__global__ void __launch_bounds__(kThreads) gemv_tiles_kernel(const uint8_t* __restrict__ W,
+__global__ void __launch_bounds__(kThreads, 2) gemv_tiles_kernel(const uint8_t* __restrict__ W,
                                                               const float* __restrict__ x,
                                                               float* __restrict__ y, int64_t N, int64_t K) {
     constexpr int TR = kItemRows;
