@@ -353,3 +353,32 @@ def test_compute_graph_fuses_nodes_sharing_x(cuda, G, O):
                 check_parity(got[i], O.gemv(shapes[i][1], raws[i], shapes[i][0], K, x), f"fused node {i} rep {rep}")
             check_parity(got[3], O.gemv(G.Q4_K, raws[3], shapes[3][0], K, got[0]), f"consumer rep {rep}")
         buf.free()
+
+
+@pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q4_0"])
+def test_compute_graph_m_rows_with_resident_weights(cuda, G, O, name):
+    """M > 1 (prefill rows) is claimed for weights resident in a B200 buffer,
+    as the reference's ggml path claims it for its own buffers
+    (src/ggml-xdna.cpp:81-93, 109-111); each row of the output matches the
+    oracle.  Host-resident weights stay M == 1 only."""
+    t = G.CLAIMED[name]
+    N, K, M = 256, 1024, 3
+    raw = O.quantize(t, normal_weights(N, K, seed=70))
+    X = np.stack([normal_x(K, seed=71 + m) for m in range(M)]).astype(np.float32)
+    with G.Backend(0) as be:
+        host_w = G.tensor(t, [K, N, 1, 1], data=_np_ptr(raw))
+        xt_h = G.tensor(G.F32, [K, M, 1, 1], data=_np_ptr(X))
+        assert not be.supports_op(G.mul_mat_node(host_w, xt_h, None, N, M))
+        buf = G.Buffer(raw.nbytes + 8192, dev=0)
+        w = buf.alloc(G.tensor(t, [K, N, 1, 1]))
+        buf.set(w, _np_ptr(raw), 0, raw.nbytes)
+        d_x = to_dev(cuda, X)
+        d_y = cuda.full((M, N), float("nan"), dtype=cuda.float32, device="cuda")
+        xt = G.tensor(G.F32, [K, M, 1, 1], data=d_x.data_ptr())
+        node = G.mul_mat_node(w, xt, d_y.data_ptr(), N, M)
+        assert be.supports_op(node)
+        assert be.compute([node]), G.last_error()
+        Y = d_y.cpu().numpy()
+        for m in range(M):
+            check_parity(Y[m], O.gemv(t, raw, N, K, X[m]), f"{name} row {m}")
+        buf.free()

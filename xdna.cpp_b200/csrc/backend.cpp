@@ -225,6 +225,15 @@ BufferRegistry& registry() {
     return r;
 }
 
+// Weights written into one of this backend's device buffers (repacked there).
+bool resident_weights(const void* data) {
+    Buffer* b = data ? registry().find(data) : nullptr;
+    if (!b || b->buft->host) return false;
+    std::lock_guard<std::mutex> lk(b->mtx);
+    auto it = b->tensors.find(reinterpret_cast<uintptr_t>(data));
+    return it != b->tensors.end() && it->second.packed;
+}
+
 BufferType* buft_instance(int dev, bool host) {
     static std::mutex m;
     static std::map<std::pair<int, bool>, std::unique_ptr<BufferType>> all;
@@ -560,9 +569,14 @@ bool row_bytes_for(int type, int64_t K, size_t* rb) {
     return true;
 }
 
-// Same predicate as the reference's supports_op_impl (src/ggml-xdna.cpp:95-147)
-// for the compat ABI, where the loader-probe relaxation never applies: MUL_MAT,
-// F32 src1, M == 1, N >= 32, N % 4 == 0, K a block multiple, packed rows.
+bool resident_weights(const void* data);
+
+// Same predicate as the reference's supports_op_impl (src/ggml-xdna.cpp:95-147):
+// MUL_MAT, F32 src1, N >= 32, N % 4 == 0, K a block multiple, packed rows, and
+// M == 1 -- except for weights that already live in this backend's device
+// buffers, which the reference's ggml path also claims for any M
+// (is_tensor_loader_probe, :81-93, :109-111): a host cannot run those rows
+// itself, and the executor loops over the M activation rows.
 bool supports_mul_mat(const ggml_tensor_xdna* op) {
     if (!op || op->op != GGML_OP_MUL_MAT) return false;
     const ggml_tensor_xdna* src0 = op->src[0];
@@ -570,7 +584,8 @@ bool supports_mul_mat(const ggml_tensor_xdna* op) {
     if (!src0 || !src1) return false;
     if (src1->type != GGML_TYPE_F32) return false;
     const int64_t K = src0->ne[0], N = src0->ne[1], M = src1->ne[1];
-    if (M != 1 || N < 32 || N % 4 != 0) return false;
+    if (N < 32 || N % 4 != 0) return false;
+    if (M != 1 && !(M > 1 && resident_weights(src0->data))) return false;
     size_t rb = 0;
     if (!type_supported(src0->type) || !row_bytes_for(src0->type, K, &rb)) return false;
     return src0->nb[1] == 0 || src0->nb[1] == rb;
