@@ -919,7 +919,7 @@ bool fusable(Backend* be, const ggml_tensor_xdna* node, FusableNode* out) {
     if (src1->ne[1] != 1 || src1->ne[0] != K || layout_kind(src0->type, N, K) != 1) return false;
     for (int d = 2; d < 4; ++d)
         if (node->ne[d] > 1 || src0->ne[d] > 1 || src1->ne[d] > 1) return false;
-    const size_t rb = static_cast<size_t>(K / 256) * 144;
+    const size_t rb = static_cast<size_t>(K / 256) * mma_row_group_bytes(src0->type);
     if (src0->nb[1] != 0 && src0->nb[1] != rb) return false;
     if ((reinterpret_cast<uintptr_t>(src1->data) & 15u) || !is_device_pointer(src1->data) ||
         !is_device_pointer(node->data))
@@ -1603,15 +1603,16 @@ static int host_repack(int type, const void* src, void* dst, int64_t n, int64_t 
         return -1;
     }
     if (layout_kind(type, n, k) == 1) {
-        const size_t rb = static_cast<size_t>(k / 256) * 144;
+        const size_t rb = static_cast<size_t>(k / 256) * mma_row_group_bytes(type);
+        const size_t gb = static_cast<size_t>(mma_group_bytes(type));
         for (int64_t t = 0; t < n / MMA_TILE_ROWS; ++t)
             for (int64_t gi = 0; gi < k / 256; ++gi) {
                 const size_t tb = static_cast<size_t>(t) * MMA_TILE_ROWS * rb;
                 if (pack)
                     mma_pack_group(type, static_cast<const uint8_t*>(src) + tb, rb, gi,
-                                   static_cast<uint8_t*>(dst) + tb + gi * MMA_GROUP_BYTES);
+                                   static_cast<uint8_t*>(dst) + tb + gi * gb);
                 else
-                    mma_unpack_group(type, static_cast<const uint8_t*>(src) + tb + gi * MMA_GROUP_BYTES, rb, gi,
+                    mma_unpack_group(type, static_cast<const uint8_t*>(src) + tb + gi * gb, rb, gi,
                                      static_cast<uint8_t*>(dst) + tb);
             }
         return 0;

@@ -345,23 +345,53 @@ XB_HD void unrepack_one(const Geometry& g, int tr, int r, int64_t b, const uint8
 // ---------------------------------------------------------------------------
 constexpr int MMA_TILE_ROWS = 16;
 constexpr int MMA_MAX_SEGMENTS = 4;  // matrices sharing x in one MMA GEMV launch
-constexpr int MMA_GROUP_BYTES = 2304;
+constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
+
+// Q5_K adds a 512-byte high-bit plane between the nibbles and the header:
+//   [0, 2048)    nibbles, as Q4_K;
+//   [2048, 2560) per lane 16 B, word i for chunks 2i and 2i+1: bit 8j + 4 + k
+//                (chunk 2i) or 8j + k (chunk 2i+1) is the fifth bit of value j
+//                of A register k (a0 row g / a1 row g+8 of block t, a2 / a3 of
+//                block t+4), so one shift and one mask put it at bit 4;
+//   [2560, 2816) the 16 rows' 16-byte headers, as Q4_K.
+XB_HD int mma_group_bytes(int type) { return type == T_Q5_K ? 2816 : MMA_GROUP_BYTES; }
+XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : 2048; }
+// GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
+XB_HD int mma_row_group_bytes(int type) { return type == T_Q5_K ? 176 : 144; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
-    return ((type == T_Q4_0 || type == T_Q4_K) && N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0) ? 1 : 0;
+    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K) && N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 &&
+            K % 256 == 0)
+               ? 1
+               : 0;
 }
 
-// 4-bit quant of (row r of a GGUF row pointer, value v of the 256-value group gi)
-XB_HD uint32_t q4_of(int type, const uint8_t* row, int64_t gi, int v) {
-    if (type == T_Q4_K) {
-        const uint8_t* qs = row + gi * 144 + 16;
-        const int j = v >> 5, o = v & 31;
-        return (qs[32 * (j >> 1) + o] >> (4 * (j & 1))) & 0xFu;
+// Byte and bit of the low 4 bits of value v (0..255) in a row's group gi:
+// Q4_K / Q5_K super-blocks keep 64-value pairs of sub-blocks in 32 bytes (low
+// nibbles = sub-block 2i, high = 2i+1); Q4_0 blocks keep value o (high nibble
+// for o >= 16) in byte o % 16 after the 2-byte scale.
+XB_HD const uint8_t* q4_byte(int type, const uint8_t* row, int64_t gi, int v, int* shift) {
+    if (type == T_Q4_0) {
+        const int o = v & 31;
+        *shift = 4 * (o >> 4);
+        return row + (gi * 8 + (v >> 5)) * 18 + 2 + (o & 15);
     }
-    const uint8_t* blk = row + (gi * 8 + (v >> 5)) * 18;  // Q4_0
-    const int o = v & 31;
-    return (blk[2 + (o & 15)] >> (4 * (o >> 4))) & 0xFu;
+    const int qs = type == T_Q5_K ? 48 : 16;
+    *shift = 4 * ((v >> 5) & 1);
+    return row + gi * mma_row_group_bytes(type) + qs + 32 * (v >> 6) + (v & 31);
 }
+XB_HD uint32_t q4_of(int type, const uint8_t* row, int64_t gi, int v) {
+    int sh;
+    const uint8_t* p = q4_byte(type, row, gi, v, &sh);
+    return (*p >> sh) & 0xFu;
+}
+// Q5_K fifth bit of value v: qh[v % 32] bit 2 * (v / 64) + (v / 32) % 2
+XB_HD const uint8_t* q5_hbyte(const uint8_t* row, int64_t gi, int v, int* bit) {
+    *bit = 2 * (v >> 6) + ((v >> 5) & 1);
+    return row + gi * 176 + 16 + (v & 31);
+}
+// bit of Q5_K high-plane word (chunk c, A register k, value j)
+XB_HD int q5_plane_bit(int c, int k, int j) { return 8 * j + ((c & 1) ? 0 : 4) + k; }
 
 // One group (gi) of one 16-row tile: GGUF rows (tile row 0 at `raw`, stride
 // row_bytes) -> MMA layout at `out` (2304 bytes), or the inverse.
@@ -381,9 +411,29 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
                 put32(out + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * kind, w);
             }
     }
-    uint8_t* hdr = out + 2048;
-    if (type == T_Q4_K) {
-        for (int r = 0; r < 16; ++r) copy_bytes(hdr + 16 * r, raw + r * row_bytes + gi * 144, 16);
+    if (type == T_Q5_K) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int i = 0; i < 4; ++i) {
+                uint32_t w = 0;
+                for (int c = 2 * i; c < 2 * i + 2; ++c)
+                    for (int k = 0; k < 4; ++k) {
+                        const uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                        const int blk = t + 4 * (k >> 1);
+                        for (int j = 0; j < 4; ++j) {
+                            int bit;
+                            const uint8_t* hb = q5_hbyte(row, gi, 32 * blk + 4 * c + j, &bit);
+                            w |= static_cast<uint32_t>((*hb >> bit) & 1u) << q5_plane_bit(c, k, j);
+                        }
+                    }
+                put32(out + 2048 + lane * 16 + 4 * i, w);
+            }
+        }
+    }
+    uint8_t* hdr = out + mma_header_off(type);
+    if (type == T_Q4_K || type == T_Q5_K) {
+        for (int r = 0; r < 16; ++r)
+            copy_bytes(hdr + 16 * r, raw + r * row_bytes + gi * mma_row_group_bytes(type), 16);
     } else {
         for (int g = 0; g < 8; ++g)
             for (int t = 0; t < 4; ++t)
@@ -395,9 +445,10 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 }
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
-    const uint8_t* hdr = in + 2048;
-    if (type == T_Q4_K) {
-        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 144, hdr + 16 * r, 16);
+    const uint8_t* hdr = in + mma_header_off(type);
+    if (type == T_Q4_K || type == T_Q5_K) {
+        for (int r = 0; r < 16; ++r)
+            copy_bytes(raw + r * row_bytes + gi * mma_row_group_bytes(type), hdr + 16 * r, 16);
     } else {
         for (int g = 0; g < 8; ++g)
             for (int t = 0; t < 4; ++t)
@@ -418,18 +469,17 @@ XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int6
                     for (int half = 0; half < 2; ++half) {
                         uint8_t* row = raw + (g + 8 * half) * row_bytes;
                         const uint32_t q = (b >> (4 * half)) & 0xFu;
-                        uint8_t* p;
                         int sh;
-                        if (type == T_Q4_K) {
-                            const int jj = v >> 5, o = v & 31;
-                            p = row + gi * 144 + 16 + 32 * (jj >> 1) + o;
-                            sh = 4 * (jj & 1);
-                        } else {
-                            const int o = v & 31;
-                            p = row + (gi * 8 + (v >> 5)) * 18 + 2 + (o & 15);
-                            sh = 4 * (o >> 4);
-                        }
+                        uint8_t* p = const_cast<uint8_t*>(q4_byte(type, row, gi, v, &sh));
                         *p = uint8_t((*p & ~(0xFu << sh)) | (q << sh));
+                        if (type == T_Q5_K) {
+                            const int k = half + 2 * kind;
+                            const uint32_t hw = get32(in + 2048 + lane * 16 + 4 * (c >> 1));
+                            int bit;
+                            uint8_t* hb = const_cast<uint8_t*>(q5_hbyte(row, gi, v, &bit));
+                            const uint32_t hv = (hw >> q5_plane_bit(c, k, j)) & 1u;
+                            *hb = uint8_t((*hb & ~(1u << bit)) | (hv << bit));
+                        }
                     }
                 }
             }

@@ -1,4 +1,4 @@
-// Integer tensor-core GEMV for 4-bit linear formats (Q4_0, Q4_K) on sm_100a.
+// Integer tensor-core GEMV for the linear 4- and 5-bit formats (Q4_0, Q4_K, Q5_K) on sm_100a.
 //
 // Why tensor cores for an M = 1 GEMV: the contraction is bandwidth bound, but
 // unpacking and multiplying 4-bit weights on the FP32 pipes costs ~4
@@ -224,10 +224,17 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+// bytes of one (16-row tile, 256-value group) unit of format TYPE
+template <int TYPE>
+constexpr int kUnitBytes = TYPE == T_Q5_K ? 2816 : MMA_GROUP_BYTES;
+template <int TYPE>
+constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
+
+template <int TYPE>
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
     const int64_t tile = u / a.ngroups;
     const SegRef r = seg_ref(a, tile);
-    return r.W + ((tile - r.first_tile) * a.ngroups + (u - tile * a.ngroups)) * MMA_GROUP_BYTES;
+    return r.W + ((tile - r.first_tile) * a.ngroups + (u - tile * a.ngroups)) * kUnitBytes<TYPE>;
 }
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
@@ -252,11 +259,12 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
     uint4 A[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
-    uint4 h0, h8;
+    uint4 h0, h8, H;
     uint2 d4;
-    if (TYPE == T_Q4_K) {
-        h0 = ld_stream(gb + 2048 + 16 * g);
-        h8 = ld_stream(gb + 2048 + 16 * (g + 8));
+    if (TYPE == T_Q5_K) H = ld_stream(gb + 2048 + lane * 16);  // fifth bits
+    if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+        h0 = ld_stream(gb + kHeaderOff<TYPE> + 16 * g);
+        h8 = ld_stream(gb + kHeaderOff<TYPE> + 16 * (g + 8));
     } else {
         d4 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + lane);
     }
@@ -270,9 +278,24 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
         const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
         const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
-        // rows g+8 stay in the high nibble: A = 16 q, undone in the combine below
-        const uint32_t a0 = w0 & 0x0F0F0F0Fu, a1 = w0 & 0xF0F0F0F0u;
-        const uint32_t a2 = w1 & 0x0F0F0F0Fu, a3 = w1 & 0xF0F0F0F0u;
+        uint32_t a0, a1, a2, a3;
+        if (TYPE == T_Q5_K) {
+            // 5-bit q: the fifth bit of register k sits at bit 4 (+k) or 0 (+k)
+            // of each byte of the chunk pair's plane word
+            const uint32_t hw = word(H, c >> 1);
+            const uint32_t e0 = (c & 1) ? (hw << 4) : hw, e1 = (c & 1) ? (hw << 3) : (hw >> 1);
+            const uint32_t e2 = (c & 1) ? (hw << 2) : (hw >> 2), e3 = (c & 1) ? (hw << 1) : (hw >> 3);
+            a0 = (w0 & 0x0F0F0F0Fu) | (e0 & 0x10101010u);
+            a1 = ((w0 >> 4) & 0x0F0F0F0Fu) | (e1 & 0x10101010u);
+            a2 = (w1 & 0x0F0F0F0Fu) | (e2 & 0x10101010u);
+            a3 = ((w1 >> 4) & 0x0F0F0F0Fu) | (e3 & 0x10101010u);
+        } else {
+            // rows g+8 stay in the high nibble: A = 16 q, undone in the combine below
+            a0 = w0 & 0x0F0F0F0Fu;
+            a1 = w0 & 0xF0F0F0F0u;
+            a2 = w1 & 0x0F0F0F0Fu;
+            a3 = w1 & 0xF0F0F0F0u;
+        }
         mma_u8s8(C[0], a0, a1, a2, a3, q.x, q.y);
         mma_u8s8(C[1], a0, a1, a2, a3, q.z, q.w);
         mma_u8s8(C[2], a0, a1, a2, a3, r.x, r.y);
@@ -282,14 +305,22 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
     // carry a factor 16 in every plane (C0 a multiple of 16, so >> 4 is exact);
     // |C2| <= 32 * 240 * 64, so C2 * 4096 < 2^31 as well.
     float T[4];
-    T[0] = static_cast<float>(C[2][0] * 65536 + C[1][0] * 256 + C[0][0]);
-    T[1] = static_cast<float>(C[2][1] * 65536 + C[1][1] * 256 + C[0][1]);
-    T[2] = static_cast<float>(C[2][2] * 4096 + C[1][2] * 16 + (C[0][2] >> 4));
-    T[3] = static_cast<float>(C[2][3] * 4096 + C[1][3] * 16 + (C[0][3] >> 4));
+    if (TYPE == T_Q5_K) {
+        // |sum| can reach 32 * 31 * 2^22 > 2^31: join the planes in F32 (the
+        // C2 term and the C1/C0 part are each exact; one rounding in the add)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+    } else {
+        T[0] = static_cast<float>(C[2][0] * 65536 + C[1][0] * 256 + C[0][0]);
+        T[1] = static_cast<float>(C[2][1] * 65536 + C[1][1] * 256 + C[0][1]);
+        T[2] = static_cast<float>(C[2][2] * 4096 + C[1][2] * 16 + (C[0][2] >> 4));
+        T[3] = static_cast<float>(C[2][3] * 4096 + C[1][3] * 16 + (C[0][3] >> 4));
+    }
     const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     const float2 xs2 = __ldg(reinterpret_cast<const float2*>(xs_) + t);
     const float s0 = sc2.x, s1 = sc2.y, x0 = xs2.x, x1 = xs2.y;
-    if (TYPE == T_Q4_K) {
+    if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
         // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four per word
         const int sh = 16 * (t & 1);
         float sc[2][2], mn[2][2], d[2], dm[2];
@@ -335,7 +366,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     __syncthreads();
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
-        for (int d = 0; d < kPrefetch && u0 + d < u1; ++d) prefetch_l2(unit_weights(a, u0 + d), MMA_GROUP_BYTES);
+        for (int d = 0; d < kPrefetch && u0 + d < u1; ++d)
+            prefetch_l2(unit_weights<TYPE>(a, u0 + d), kUnitBytes<TYPE>);
     pdl_release();
     pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel
 
@@ -351,14 +383,14 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         int pf_end;  // a matrix's tiles are contiguous: prefetch ahead up to its last unit
         {
             const SegRef sr = seg_ref(a, tile);
-            tw = sr.W + static_cast<int64_t>(tile - static_cast<int>(sr.first_tile)) * ng * MMA_GROUP_BYTES;
+            tw = sr.W + static_cast<int64_t>(tile - static_cast<int>(sr.first_tile)) * ng * kUnitBytes<TYPE>;
             pf_end = (static_cast<int>(sr.end_tile) - tile) * ng;
         }
         float y0 = 0.f, y8 = 0.f;
         for (int gi = u - tbeg; gi < gend; ++gi) {
             if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
-                prefetch_l2(tw + (gi + kPrefetch) * MMA_GROUP_BYTES, MMA_GROUP_BYTES);
-            group_dot<TYPE>(tw + gi * MMA_GROUP_BYTES, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g, t,
+                prefetch_l2(tw + (gi + kPrefetch) * kUnitBytes<TYPE>, kUnitBytes<TYPE>);
+            group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g, t,
                             y0, y8);
         }
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
@@ -631,10 +663,38 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
 
 size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
+// One thread per (tile, group) through the shared host/device routines of
+// formats.cuh: the repack path of the 5-bit layout (a one-time upload cost).
+template <bool kPack>
+__global__ void __launch_bounds__(128) mma_repack_generic_kernel(int type, const uint8_t* __restrict__ src,
+                                                                 uint8_t* __restrict__ dst, int64_t K, int64_t ntiles) {
+    const int64_t ngroups = K / 256, row_bytes = ngroups * mma_row_group_bytes(type);
+    const int64_t gb = mma_group_bytes(type);
+    for (int64_t item = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; item < ntiles * ngroups;
+         item += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t tile = item / ngroups, gi = item % ngroups;
+        const int64_t tbase = tile * MMA_TILE_ROWS * row_bytes;
+        if (kPack)
+            mma_pack_group(type, src + tbase, row_bytes, gi, dst + tbase + gi * gb);
+        else
+            mma_unpack_group(type, src + tbase + gi * gb, row_bytes, gi, dst + tbase);
+    }
+}
+
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
+    if (type == T_Q5_K) {
+        const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
+        if (pack)
+            mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
+                type, static_cast<const uint8_t*>(raw), static_cast<uint8_t*>(packed), K, ntiles);
+        else
+            mma_repack_generic_kernel<false><<<unsigned(blocks), 128, 0, stream>>>(
+                type, static_cast<const uint8_t*>(raw), static_cast<uint8_t*>(packed), K, ntiles);
+        return cudaGetLastError();
+    }
     const int64_t blocks = (items + 3) / 4 < 65536 ? (items + 3) / 4 : 65536;
     if (pack)
         mma_repack_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(type, static_cast<const uint8_t*>(raw),
@@ -653,7 +713,8 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
-    if ((type != T_Q4_K && type != T_Q4_0) || nseg < 1 || nseg > kMaxSegs) return cudaErrorInvalidValue;
+    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K) || nseg < 1 || nseg > kMaxSegs)
+        return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
         return cudaErrorInvalidValue;
     GemvArgs a = {};
@@ -730,6 +791,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cg.attrs = attr2;
     cg.numAttrs = 1;
     if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
+    if (type == T_Q5_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q5_K>, a);
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
