@@ -354,16 +354,48 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //                of A register k (a0 row g / a1 row g+8 of block t, a2 / a3 of
 //                block t+4), so one shift and one mask put it at bit 4;
 //   [2560, 2816) the 16 rows' 16-byte headers, as Q4_K.
-XB_HD int mma_group_bytes(int type) { return type == T_Q5_K ? 2816 : MMA_GROUP_BYTES; }
-XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : 2048; }
+//
+// Q6_K (16-value sub-blocks with int8 scales; 6-bit q) uses 16-value B
+// blocks: chunk cc (0..7) covers values 4 (cc % 4) .. +3 of the 16-value
+// blocks 8 (cc / 4) + column, so chunks 0-3 and 4-7 are two sets of 8 blocks.
+//   [0, 2048)    low nibbles, swizzled as Q4_K (column t / t+4 of each chunk);
+//   [2048, 3072) per lane 32 B: word cc holds the high two bits of value j of
+//                A register k at bits 8j + 2k, 8j + 2k + 1;
+//   [3072, 3328) per lane 8 int8 scales: rows g, g+8 (4 bytes each) x sets 0, 1
+//                (2 bytes each) x blocks 2t, 2t+1 of the set;
+//   [3328, 3360) the 16 rows' fp16 d.
+XB_HD int mma_group_bytes(int type) {
+    return type == T_Q5_K ? 2816 : (type == T_Q6_K ? 3360 : MMA_GROUP_BYTES);
+}
+XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : (type == T_Q6_K ? 3072 : 2048); }
 // GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
-XB_HD int mma_row_group_bytes(int type) { return type == T_Q5_K ? 176 : 144; }
+XB_HD int mma_row_group_bytes(int type) { return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : 144); }
+// x blocks (B columns) of 16 values instead of 32
+XB_HD bool mma_blk16(int type) { return type == T_Q6_K; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
-    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K) && N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 &&
-            K % 256 == 0)
+    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) && N > 0 && K > 0 &&
+            N % MMA_TILE_ROWS == 0 && K % 256 == 0)
                ? 1
                : 0;
+}
+
+// value index (0..255) of lane (g, t)'s A register `kind` (0: column t,
+// 1: column t + 4), chunk c, byte j
+XB_HD int mma_value(int type, int c, int t, int kind, int j) {
+    if (mma_blk16(type)) return 16 * (8 * (c >> 2) + t + 4 * kind) + 4 * (c & 3) + j;
+    return 32 * (t + 4 * kind) + 4 * c + j;
+}
+// Q6_K: low nibble byte / shift and high-pair byte / shift of value v
+XB_HD const uint8_t* q6_lo(const uint8_t* row, int64_t gi, int v, int* shift) {
+    const int n = v >> 7, qd = (v >> 5) & 3, l = v & 31;
+    *shift = 4 * (qd >> 1);
+    return row + gi * 210 + 64 * n + l + 32 * (qd & 1);
+}
+XB_HD const uint8_t* q6_hi(const uint8_t* row, int64_t gi, int v, int* shift) {
+    const int n = v >> 7, qd = (v >> 5) & 3, l = v & 31;
+    *shift = 2 * qd;
+    return row + gi * 210 + 128 + 32 * n + l;
 }
 
 // Byte and bit of the low 4 bits of value v (0..255) in a row's group gi:
@@ -371,6 +403,7 @@ XB_HD int layout_kind(int type, int64_t N, int64_t K) {
 // nibbles = sub-block 2i, high = 2i+1); Q4_0 blocks keep value o (high nibble
 // for o >= 16) in byte o % 16 after the 2-byte scale.
 XB_HD const uint8_t* q4_byte(int type, const uint8_t* row, int64_t gi, int v, int* shift) {
+    if (type == T_Q6_K) return q6_lo(row, gi, v, shift);
     if (type == T_Q4_0) {
         const int o = v & 31;
         *shift = 4 * (o >> 4);
@@ -402,14 +435,37 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
         const uint8_t* r8 = raw + (g + 8) * row_bytes;
         for (int c = 0; c < 8; ++c)
             for (int kind = 0; kind < 2; ++kind) {
-                const int blk = t + 4 * kind;
                 uint32_t w = 0;
                 for (int j = 0; j < 4; ++j) {
-                    const int v = 32 * blk + 4 * c + j;
+                    const int v = mma_value(type, c, t, kind, j);
                     w |= (q4_of(type, r0, gi, v) | (q4_of(type, r8, gi, v) << 4)) << (8 * j);
                 }
                 put32(out + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * kind, w);
             }
+    }
+    if (type == T_Q6_K) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c) {
+                uint32_t w = 0;
+                for (int k = 0; k < 4; ++k) {
+                    const uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    for (int j = 0; j < 4; ++j) {
+                        int sh;
+                        const uint8_t* hb = q6_hi(row, gi, mma_value(type, c, t, k >> 1, j), &sh);
+                        w |= static_cast<uint32_t>((*hb >> sh) & 3u) << (8 * j + 2 * k);
+                    }
+                }
+                put32(out + 2048 + lane * 32 + 4 * c, w);
+            }
+            for (int h = 0; h < 2; ++h)
+                for (int st = 0; st < 2; ++st)
+                    for (int b = 0; b < 2; ++b)
+                        out[3072 + lane * 8 + 4 * h + 2 * st + b] =
+                            raw[(g + 8 * h) * row_bytes + gi * 210 + 192 + 8 * st + 2 * t + b];
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(out + 3328 + 2 * r, raw + r * row_bytes + gi * 210 + 208, 2);
+        return;
     }
     if (type == T_Q5_K) {
         for (int lane = 0; lane < 32; ++lane) {
@@ -446,7 +502,29 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
     const uint8_t* hdr = in + mma_header_off(type);
-    if (type == T_Q4_K || type == T_Q5_K) {
+    if (type == T_Q6_K) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int h = 0; h < 2; ++h)
+                for (int st = 0; st < 2; ++st)
+                    for (int b = 0; b < 2; ++b)
+                        raw[(g + 8 * h) * row_bytes + gi * 210 + 192 + 8 * st + 2 * t + b] =
+                            in[3072 + lane * 8 + 4 * h + 2 * st + b];
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t w = get32(in + 2048 + lane * 32 + 4 * c);
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    for (int j = 0; j < 4; ++j) {
+                        int sh;
+                        uint8_t* hb = const_cast<uint8_t*>(q6_hi(row, gi, mma_value(type, c, t, k >> 1, j), &sh));
+                        const uint32_t hv = (w >> (8 * j + 2 * k)) & 3u;
+                        *hb = uint8_t((*hb & ~(3u << sh)) | (hv << sh));
+                    }
+                }
+            }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 210 + 208, in + 3328 + 2 * r, 2);
+    } else if (type == T_Q4_K || type == T_Q5_K) {
         for (int r = 0; r < 16; ++r)
             copy_bytes(raw + r * row_bytes + gi * mma_row_group_bytes(type), hdr + 16 * r, 16);
     } else {
@@ -461,10 +539,9 @@ XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int6
         const int g = lane >> 2, t = lane & 3;
         for (int c = 0; c < 8; ++c)
             for (int kind = 0; kind < 2; ++kind) {
-                const int blk = t + 4 * kind;
                 const uint32_t w = get32(in + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * kind);
                 for (int j = 0; j < 4; ++j) {
-                    const int v = 32 * blk + 4 * c + j;
+                    const int v = mma_value(type, c, t, kind, j);
                     const uint32_t b = (w >> (8 * j)) & 0xFFu;
                     for (int half = 0; half < 2; ++half) {
                         uint8_t* row = raw + (g + 8 * half) * row_bytes;

@@ -106,6 +106,10 @@ __device__ __forceinline__ uint32_t digit_word(uint32_t v0, uint32_t v1, uint32_
 
 // x preparation: one warp per 32-value block (lane j = value j); also zeroes
 // the tile counters of the GEMV that follows.
+// BL = values per x block (B column): 32, or 16 for the formats with
+// 16-value sub-blocks (chunks 0-3 then cover blocks 0-7, chunks 4-7 blocks
+// 8-15 of the group).
+template <int BL>
 __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ frags,
                                                     uint8_t* __restrict__ zeros, float* __restrict__ scale,
                                                     float* __restrict__ xsum, int* __restrict__ count,
@@ -117,12 +121,13 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
     for (int64_t i = gtid; i < ntiles; i += nthr) count[i] = 0;
     if (gtid < kSlotBytes / 4) reinterpret_cast<uint32_t*>(zeros)[gtid] = 0u;
     const int lane = threadIdx.x & 31;
-    const int64_t nblk = K / 32;
-    for (int64_t b = gtid >> 5; b < nblk; b += nthr >> 5) {
-        const float v = x[b * 32 + lane];
+    const int64_t nw = K / 32;  // one warp per 32 values (32 / BL blocks)
+    for (int64_t w32 = gtid >> 5; w32 < nw; w32 += nthr >> 5) {
+        const int64_t b = (w32 * 32 + lane) / BL;  // this lane's block
+        const float v = x[w32 * 32 + lane];
         float m = fabsf(v), s = v;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
+        for (int o = BL / 2; o > 0; o >>= 1) {
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
             s += __shfl_xor_sync(0xffffffffu, s, o);
         }
@@ -140,12 +145,15 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
         const uint32_t n1 = __shfl_down_sync(0xffffffffu, mine, 1);
         const uint32_t n2 = __shfl_down_sync(0xffffffffu, mine, 2);
         const uint32_t n3 = __shfl_down_sync(0xffffffffu, mine, 3);
-        if ((lane & 3) == 0) {  // values 4c .. 4c + 3 of chunk c = lane / 4
+        if ((lane & 3) == 0) {  // values 4c' .. 4c' + 3 of the block, c' = (lane % BL) / 4
             const uint32_t D0 = digit_word(mine, n1, n2, n3, 0);
             const uint32_t D1 = digit_word(mine, n1, n2, n3, 1);
             const uint32_t D2 = digit_word(mine, n1, n2, n3, 2);
-            const int64_t gi = b >> 3;
-            const int blk = static_cast<int>(b & 7), c = lane >> 2;
+            constexpr int kPerGroup = 256 / BL;
+            const int64_t gi = b / kPerGroup;
+            const int jb = static_cast<int>(b % kPerGroup);
+            const int blk = jb & 7;                                       // B column
+            const int c = (BL == 32 ? 0 : 4 * (jb >> 3)) + (lane % BL) / 4;  // chunk
             uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
             if (blk < 4) {
                 slot[0] = make_uint4(D0, 0u, D1, 0u);
@@ -155,7 +163,7 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
                 slot[1] = make_uint4(0u, D2, 0u, 0u);
             }
         }
-        if (lane == 0) {
+        if (lane % BL == 0) {
             scale[b] = ldexpf(1.0f, e);
             xsum[b] = s;
         }
@@ -226,9 +234,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 // bytes of one (16-row tile, 256-value group) unit of format TYPE
 template <int TYPE>
-constexpr int kUnitBytes = TYPE == T_Q5_K ? 2816 : MMA_GROUP_BYTES;
+constexpr int kUnitBytes = TYPE == T_Q5_K ? 2816 : (TYPE == T_Q6_K ? 3360 : MMA_GROUP_BYTES);
 template <int TYPE>
 constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
+template <int TYPE>
+constexpr int kXBlocks = TYPE == T_Q6_K ? 16 : 8;  // x blocks (scales, sums) per 256 values
 
 template <int TYPE>
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
@@ -252,10 +262,68 @@ __device__ __forceinline__ int64_t warp_of(int64_t u, int64_t U, int64_t NW) { r
 
 // One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
 // fb: this lane's B slot of chunk 0 (or the zero slot), fc: bytes between chunks.
+// Q6_K: two sets of 8 sixteen-value blocks; q = 6 bits (A = q, u8), value =
+// d * sc * (q - 32) with int8 sc per 16 values, so each block adds
+// d * sc * (2^e * T - 32 * xsum).
+__device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* fb, int fc,
+                                              const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
+                                              int g, int t, float& y0, float& y8) {
+    uint4 A[4], H[2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
+    H[0] = ld_stream(gb + 2048 + lane * 32);
+    H[1] = ld_stream(gb + 2048 + lane * 32 + 16);
+    const uint2 scw = __ldg(reinterpret_cast<const uint2*>(gb + 3072) + lane);
+    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 3328) + g));
+    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 3328) + g + 8));
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+        int C[3][4];
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+        for (int cs = 0; cs < 4; ++cs) {
+            const int c = 4 * st + cs;
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+            const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+            const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
+            const uint32_t hw = word(H[c >> 2], c & 3);  // bits 8j + 2k: high pair of register k
+            const uint32_t a0 = (w0 & 0x0F0F0F0Fu) | ((hw << 4) & 0x30303030u);
+            const uint32_t a1 = ((w0 >> 4) & 0x0F0F0F0Fu) | ((hw << 2) & 0x30303030u);
+            const uint32_t a2 = (w1 & 0x0F0F0F0Fu) | (hw & 0x30303030u);
+            const uint32_t a3 = ((w1 >> 4) & 0x0F0F0F0Fu) | ((hw >> 2) & 0x30303030u);
+            mma_u8s8(C[0], a0, a1, a2, a3, q.x, q.y);
+            mma_u8s8(C[1], a0, a1, a2, a3, q.z, q.w);
+            mma_u8s8(C[2], a0, a1, a2, a3, r.x, r.y);
+        }
+        // |sum| <= 16 * 63 * 2^22 may pass 2^31: join the planes in F32
+        float T[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
+        const float2 xs2 = reinterpret_cast<const float2*>(xs_ + 8 * st)[t];
+        const uint32_t sg = (st ? scw.x >> 16 : scw.x), s8 = (st ? scw.y >> 16 : scw.y);
+        const float kg0 = static_cast<float>(static_cast<int8_t>(sg & 0xFFu));
+        const float kg1 = static_cast<float>(static_cast<int8_t>((sg >> 8) & 0xFFu));
+        const float k80 = static_cast<float>(static_cast<int8_t>(s8 & 0xFFu));
+        const float k81 = static_cast<float>(static_cast<int8_t>((s8 >> 8) & 0xFFu));
+        const float b0 = fmaf(-32.0f, xs2.x, 0.0f), b1 = -32.0f * xs2.y;
+        y0 = fmaf(dg, fmaf(kg0, fmaf(sc2.x, T[0], b0), kg1 * fmaf(sc2.y, T[1], b1)), y0);
+        y8 = fmaf(d8, fmaf(k80, fmaf(sc2.x, T[2], b0), k81 * fmaf(sc2.y, T[3], b1)), y8);
+    }
+}
+
 template <int TYPE>
 __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
                                           const float* __restrict__ xs_, int lane, int g, int t, float& y0,
                                           float& y8) {
+    if constexpr (TYPE == T_Q6_K) {
+        group_dot_q6k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+        return;
+    }
     uint4 A[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
@@ -390,8 +458,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         for (int gi = u - tbeg; gi < gend; ++gi) {
             if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
                 prefetch_l2(tw + (gi + kPrefetch) * kUnitBytes<TYPE>, kUnitBytes<TYPE>);
-            group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * 8, a.xsum + gi * 8, lane, g, t,
-                            y0, y8);
+            group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
+                            a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
         }
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
@@ -654,8 +722,8 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
     L.frags = 0;
     L.zeros = up(L.frags + ngroups * kGroupFragBytes);
     L.scale = up(L.zeros + kSlotBytes);
-    L.xsum = up(L.scale + nblk * sizeof(float));
-    L.count = up(L.xsum + nblk * sizeof(float));
+    L.xsum = up(L.scale + 2 * nblk * sizeof(float));  // room for 16-value blocks
+    L.count = up(L.xsum + 2 * nblk * sizeof(float));
     L.partial = up(L.count + (ntiles + 1) * sizeof(int));  // + the CTA completion counter
     L.total = up(L.partial + size_t(kMaxCtas) * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
@@ -685,7 +753,7 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
-    if (type == T_Q5_K) {
+    if (type == T_Q5_K || type == T_Q6_K) {
         const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
         if (pack)
             mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
@@ -713,7 +781,7 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
-    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K) || nseg < 1 || nseg > kMaxSegs)
+    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K) || nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
         return cudaErrorInvalidValue;
@@ -775,9 +843,13 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cp.stream = stream;
     cp.attrs = attr;
     cp.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cp, xprep_kernel, x, K, base + L.frags, base + L.zeros,
-                                       reinterpret_cast<float*>(base + L.scale),
-                                       reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1);
+    cudaError_t e = mma_blk16(type)
+                        ? cudaLaunchKernelEx(&cp, xprep_kernel<16>, x, K, base + L.frags, base + L.zeros,
+                                             reinterpret_cast<float*>(base + L.scale),
+                                             reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1)
+                        : cudaLaunchKernelEx(&cp, xprep_kernel<32>, x, K, base + L.frags, base + L.zeros,
+                                             reinterpret_cast<float*>(base + L.scale),
+                                             reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1);
     if (e != cudaSuccess) return e;
 
     cudaLaunchConfig_t cg = {};
@@ -792,6 +864,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cg.numAttrs = 1;
     if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
     if (type == T_Q5_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q5_K>, a);
+    if (type == T_Q6_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q6_K>, a);
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
