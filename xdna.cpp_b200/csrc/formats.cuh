@@ -364,20 +364,60 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //   [3072, 3328) per lane 8 int8 scales: rows g, g+8 (4 bytes each) x sets 0, 1
 //                (2 bytes each) x blocks 2t, 2t+1 of the set;
 //   [3328, 3360) the 16 rows' fp16 d.
+//
+// Q3_K (3-bit q = low pair + 4 * high bit, 6-bit scales per 16 values) uses the
+// same 16-value chunk order as Q6_K:
+//   [0, 1024)    per lane 32 B: word c holds the low pair of value j of A
+//                register k at bits 8j + 2k, 8j + 2k + 1;
+//   [1024, 1536) per lane 16 B: word i holds the high bit of value j of
+//                register k of chunk 2i (bit 8j + k) and 2i + 1 (bit 8j + 4 + k);
+//   [1536, 1664) per lane 4 B: low nibbles of its 8 scales, [1664, 1728) per
+//                lane 2 B: their high pairs (scale order as Q6_K's int8 scales);
+//   [1728, 1760) the 16 rows' fp16 d.
 XB_HD int mma_group_bytes(int type) {
-    return type == T_Q5_K ? 2816 : (type == T_Q6_K ? 3360 : MMA_GROUP_BYTES);
+    return type == T_Q5_K ? 2816 : (type == T_Q6_K ? 3360 : (type == T_Q3_K ? 1760 : MMA_GROUP_BYTES));
 }
 XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : (type == T_Q6_K ? 3072 : 2048); }
 // GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
-XB_HD int mma_row_group_bytes(int type) { return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : 144); }
+XB_HD int mma_row_group_bytes(int type) {
+    return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : (type == T_Q3_K ? 110 : 144));
+}
 // x blocks (B columns) of 16 values instead of 32
-XB_HD bool mma_blk16(int type) { return type == T_Q6_K; }
+XB_HD bool mma_blk16(int type) { return type == T_Q6_K || type == T_Q3_K; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
-    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) && N > 0 && K > 0 &&
-            N % MMA_TILE_ROWS == 0 && K % 256 == 0)
+    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q3_K) && N > 0 &&
+            K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0)
                ? 1
                : 0;
+}
+
+// Q3_K: low pair / high bit of value v, and the 6-bit scale i of a row's group
+XB_HD const uint8_t* q3_lo(const uint8_t* row, int64_t gi, int v, int* shift) {
+    const int n = v >> 7, j = (v >> 5) & 3, half = (v >> 4) & 1, l = v & 15;
+    *shift = 2 * j;
+    return row + gi * 110 + 32 + 32 * n + 16 * half + l;
+}
+XB_HD const uint8_t* q3_hi(const uint8_t* row, int64_t gi, int v, int* bit) {
+    const int n = v >> 7, j = (v >> 5) & 3, half = (v >> 4) & 1, l = v & 15;
+    *bit = 4 * n + j;
+    return row + gi * 110 + 16 * half + l;
+}
+XB_HD uint32_t q3_scale(const uint8_t* row, int64_t gi, int i) {
+    const uint8_t* s12 = row + gi * 110 + 96;
+    const int q = i >> 2, r = i & 3;
+    const uint32_t lo = (s12[4 * (q & 1) + r] >> (4 * (q >> 1))) & 0xFu;
+    const uint32_t hi = (s12[8 + r] >> (2 * q)) & 3u;
+    return lo | (hi << 4);
+}
+XB_HD void q3_set_scale(uint8_t* row, int64_t gi, int i, uint32_t v) {
+    uint8_t* s12 = row + gi * 110 + 96;
+    const int q = i >> 2, r = i & 3;
+    uint8_t* pl = s12 + 4 * (q & 1) + r;
+    const int sl = 4 * (q >> 1);
+    *pl = uint8_t((*pl & ~(0xFu << sl)) | ((v & 0xFu) << sl));
+    uint8_t* ph = s12 + 8 + r;
+    *ph = uint8_t((*ph & ~(3u << (2 * q))) | (((v >> 4) & 3u) << (2 * q)));
 }
 
 // value index (0..255) of lane (g, t)'s A register `kind` (0: column t,
@@ -429,6 +469,48 @@ XB_HD int q5_plane_bit(int c, int k, int j) { return 8 * j + ((c & 1) ? 0 : 4) +
 // One group (gi) of one 16-row tile: GGUF rows (tile row 0 at `raw`, stride
 // row_bytes) -> MMA layout at `out` (2304 bytes), or the inverse.
 XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64_t gi, uint8_t* out) {
+    if (type == T_Q3_K) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c) {
+                uint32_t lw = 0;
+                for (int k = 0; k < 4; ++k) {
+                    const uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    for (int j = 0; j < 4; ++j) {
+                        int sh;
+                        const uint8_t* lb = q3_lo(row, gi, mma_value(type, c, t, k >> 1, j), &sh);
+                        lw |= static_cast<uint32_t>((*lb >> sh) & 3u) << (8 * j + 2 * k);
+                    }
+                }
+                put32(out + lane * 32 + 4 * c, lw);
+            }
+            for (int i = 0; i < 4; ++i) {
+                uint32_t hw = 0;
+                for (int c = 2 * i; c < 2 * i + 2; ++c)
+                    for (int k = 0; k < 4; ++k) {
+                        const uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                        for (int j = 0; j < 4; ++j) {
+                            int bit;
+                            const uint8_t* hb = q3_hi(row, gi, mma_value(type, c, t, k >> 1, j), &bit);
+                            hw |= static_cast<uint32_t>((*hb >> bit) & 1u) << (8 * j + 4 * (c & 1) + k);
+                        }
+                    }
+                put32(out + 1024 + lane * 16 + 4 * i, hw);
+            }
+            uint32_t lo = 0, hi = 0;
+            for (int i = 0; i < 8; ++i) {  // i = 4 h + 2 set + b
+                const int h = i >> 2, st = (i >> 1) & 1, b = i & 1;
+                const uint32_t sc = q3_scale(raw + (g + 8 * h) * row_bytes, gi, 8 * st + 2 * t + b);
+                lo |= (sc & 0xFu) << (4 * i);
+                hi |= ((sc >> 4) & 3u) << (2 * i);
+            }
+            put32(out + 1536 + 4 * lane, lo);
+            out[1664 + 2 * lane] = uint8_t(hi & 0xFFu);
+            out[1664 + 2 * lane + 1] = uint8_t(hi >> 8);
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(out + 1728 + 2 * r, raw + r * row_bytes + gi * 110 + 108, 2);
+        return;
+    }
     for (int lane = 0; lane < 32; ++lane) {
         const int g = lane >> 2, t = lane & 3;
         const uint8_t* r0 = raw + g * row_bytes;
@@ -501,6 +583,36 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 }
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
+    if (type == T_Q3_K) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t lw = get32(in + lane * 32 + 4 * c);
+                const uint32_t hw = get32(in + 1024 + lane * 16 + 4 * (c >> 1));
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    for (int j = 0; j < 4; ++j) {
+                        const int v = mma_value(type, c, t, k >> 1, j);
+                        int sh, bit;
+                        uint8_t* lb = const_cast<uint8_t*>(q3_lo(row, gi, v, &sh));
+                        *lb = uint8_t((*lb & ~(3u << sh)) | (((lw >> (8 * j + 2 * k)) & 3u) << sh));
+                        uint8_t* hb = const_cast<uint8_t*>(q3_hi(row, gi, v, &bit));
+                        const uint32_t hv = (hw >> (8 * j + 4 * (c & 1) + k)) & 1u;
+                        *hb = uint8_t((*hb & ~(1u << bit)) | (hv << bit));
+                    }
+                }
+            }
+            const uint32_t lo = get32(in + 1536 + 4 * lane);
+            const uint32_t hi = in[1664 + 2 * lane] | (uint32_t(in[1664 + 2 * lane + 1]) << 8);
+            for (int i = 0; i < 8; ++i) {
+                const int h = i >> 2, st = (i >> 1) & 1, b = i & 1;
+                q3_set_scale(raw + (g + 8 * h) * row_bytes, gi, 8 * st + 2 * t + b,
+                             ((lo >> (4 * i)) & 0xFu) | (((hi >> (2 * i)) & 3u) << 4));
+            }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 110 + 108, in + 1728 + 2 * r, 2);
+        return;
+    }
     const uint8_t* hdr = in + mma_header_off(type);
     if (type == T_Q6_K) {
         for (int lane = 0; lane < 32; ++lane) {

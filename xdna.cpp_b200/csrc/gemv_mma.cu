@@ -1,4 +1,4 @@
-// Integer tensor-core GEMV for the linear 4- and 5-bit formats (Q4_0, Q4_K, Q5_K) on sm_100a.
+// Integer tensor-core GEMV for the linear formats (Q4_0, Q3_K, Q4_K, Q5_K, Q6_K) on sm_100a.
 //
 // Why tensor cores for an M = 1 GEMV: the contraction is bandwidth bound, but
 // unpacking and multiplying 4-bit weights on the FP32 pipes costs ~4
@@ -234,11 +234,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 // bytes of one (16-row tile, 256-value group) unit of format TYPE
 template <int TYPE>
-constexpr int kUnitBytes = TYPE == T_Q5_K ? 2816 : (TYPE == T_Q6_K ? 3360 : MMA_GROUP_BYTES);
+constexpr int kUnitBytes =
+    TYPE == T_Q5_K ? 2816 : (TYPE == T_Q6_K ? 3360 : (TYPE == T_Q3_K ? 1760 : MMA_GROUP_BYTES));
 template <int TYPE>
 constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
 template <int TYPE>
-constexpr int kXBlocks = TYPE == T_Q6_K ? 16 : 8;  // x blocks (scales, sums) per 256 values
+constexpr int kXBlocks = (TYPE == T_Q6_K || TYPE == T_Q3_K) ? 16 : 8;  // x blocks (scales, sums) per 256 values
 
 template <int TYPE>
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
@@ -316,12 +317,78 @@ __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* 
     }
 }
 
+// Q3_K: two sets of 8 sixteen-value blocks; q3 = low pair + 4 * high bit
+// (A = q3, u8), value = d * (sc - 32) * (q3 - 4) with 6-bit sc per 16 values.
+__device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* fb, int fc,
+                                              const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
+                                              int g, int t, float& y0, float& y8) {
+    const uint4 L0 = ld_stream(gb + lane * 32), L1 = ld_stream(gb + lane * 32 + 16);
+    const uint4 H = ld_stream(gb + 1024 + lane * 16);
+    const uint32_t slo = __ldg(reinterpret_cast<const unsigned int*>(gb + 1536) + lane);
+    const uint32_t shi = __ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + lane);
+    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1728) + g));
+    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1728) + g + 8));
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+        int C[3][4];
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+        for (int cs = 0; cs < 4; ++cs) {
+            const int c = 4 * st + cs;
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+            const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+            const uint32_t lw = word(c < 4 ? L0 : L1, c & 3);  // bits 8j + 2k: low pair of register k
+            const uint32_t hw = word(H, c >> 1);                // bit 8j + 4 (c & 1) + k: high bit
+            uint32_t hk[4];
+            if (c & 1) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) hk[k] = hw >> (2 + k);
+            } else {
+                hk[0] = hw << 2;
+                hk[1] = hw << 1;
+                hk[2] = hw;
+                hk[3] = hw >> 1;
+            }
+            const uint32_t a0 = (lw & 0x03030303u) | (hk[0] & 0x04040404u);
+            const uint32_t a1 = ((lw >> 2) & 0x03030303u) | (hk[1] & 0x04040404u);
+            const uint32_t a2 = ((lw >> 4) & 0x03030303u) | (hk[2] & 0x04040404u);
+            const uint32_t a3 = ((lw >> 6) & 0x03030303u) | (hk[3] & 0x04040404u);
+            mma_u8s8(C[0], a0, a1, a2, a3, q.x, q.y);
+            mma_u8s8(C[1], a0, a1, a2, a3, q.z, q.w);
+            mma_u8s8(C[2], a0, a1, a2, a3, r.x, r.y);
+        }
+        // |sum| <= 16 * 7 * 2^22 < 2^31: exact in int32
+        float T[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) T[k] = static_cast<float>(C[2][k] * 65536 + C[1][k] * 256 + C[0][k]);
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
+        const float2 xs2 = reinterpret_cast<const float2*>(xs_ + 8 * st)[t];
+        float k6[4];  // scales (i = 4 h + 2 st + b) minus 32
+#pragma unroll
+        for (int hb = 0; hb < 4; ++hb) {
+            const int i = 4 * (hb >> 1) + 2 * st + (hb & 1);
+            const uint32_t v = ((slo >> (4 * i)) & 0xFu) | (((shi >> (2 * i)) & 3u) << 4);
+            k6[hb] = static_cast<float>(static_cast<int>(v) - 32);
+        }
+        const float b0 = -4.0f * xs2.x, b1 = -4.0f * xs2.y;
+        y0 = fmaf(dg, fmaf(k6[0], fmaf(sc2.x, T[0], b0), k6[1] * fmaf(sc2.y, T[1], b1)), y0);
+        y8 = fmaf(d8, fmaf(k6[2], fmaf(sc2.x, T[2], b0), k6[3] * fmaf(sc2.y, T[3], b1)), y8);
+    }
+}
+
 template <int TYPE>
 __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
                                           const float* __restrict__ xs_, int lane, int g, int t, float& y0,
                                           float& y8) {
     if constexpr (TYPE == T_Q6_K) {
         group_dot_q6k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+        return;
+    }
+    if constexpr (TYPE == T_Q3_K) {
+        group_dot_q3k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
         return;
     }
     uint4 A[4];
@@ -753,7 +820,7 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
-    if (type == T_Q5_K || type == T_Q6_K) {
+    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K) {
         const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
         if (pack)
             mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
@@ -781,7 +848,8 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
-    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K) || nseg < 1 || nseg > kMaxSegs)
+    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K) || nseg < 1 ||
+        nseg > kMaxSegs)
         return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
         return cudaErrorInvalidValue;
@@ -865,6 +933,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     if (type == T_Q4_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K>, a);
     if (type == T_Q5_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q5_K>, a);
     if (type == T_Q6_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q6_K>, a);
+    if (type == T_Q3_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q3_K>, a);
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
