@@ -191,6 +191,12 @@ int b200_repack(int type, const void *raw, void *packed, int64_t n, int64_t k, v
 int b200_unpack(int type, const void *packed, void *raw, int64_t n, int64_t k, void *stream);
 /* BF16 activations -> F32 on the device (reference run_bf16 conversion :1894-1908). */
 int b200_bf16_to_f32(const uint16_t *src, float *dst, int64_t n, void *stream);
+/* y = W x for BF16 x: exact conversion to F32 (into a per-stream device buffer
+ * that grows on demand) followed by b200_gemv.  Replaces
+ * XdnaGemvEngine::run_bf16 / run_quant_bf16 (src/xdna-gemv-engine.cpp:1894-1908,
+ * 1994-2009). */
+int b200_gemv_bf16(int type, const void *w_packed, const uint16_t *x_bf16, float *y, int64_t n, int64_t k,
+                   void *stream, int pdl);
 /* Synthetic N(0, sigma) F32 values and device quantisers (Q4_0, Q4_K). */
 int b200_fill_normal(float *out, int64_t n, uint64_t seed, float sigma, void *stream);
 int b200_quantize(int type, const float *src, void *dst, int64_t n, int64_t k, void *stream);

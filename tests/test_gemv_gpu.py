@@ -382,3 +382,25 @@ def test_compute_graph_m_rows_with_resident_weights(cuda, G, O, name):
         for m in range(M):
             check_parity(Y[m], O.gemv(t, raw, N, K, X[m]), f"{name} row {m}")
         buf.free()
+
+
+@pytest.mark.parametrize("name,N,K", [("Q4_0", 512, 256), ("Q4_K", 512, 1024), ("Q6_K", 256, 2048),
+                                      ("IQ3_S", 96, 512)])
+def test_gemv_bf16_entry(cuda, G, O, name, N, K):
+    """b200_gemv_bf16 = reference run_bf16 / run_quant_bf16 (src/xdna-gemv-engine.cpp:
+    1894-1908, 1994-2009): exact BF16 -> F32, then the same GEMV."""
+    t = G.CLAIMED[name]
+    raw = O.quantize(t, normal_weights(N, K, seed=404 + K))
+    xb = O.f32_to_bf16(normal_x(K, seed=405))
+    x = (xb.astype(np.uint32) << 16).view(np.float32)
+    stream = cuda.cuda.current_stream().cuda_stream
+    d_raw = to_dev(cuda, raw)
+    d_pk = cuda.empty_like(d_raw)
+    d_xb = to_dev(cuda, xb)
+    d_y = cuda.full((N,), float("nan"), dtype=cuda.float32, device="cuda")
+    L = G.lib()
+    G.check(L.b200_repack(t, d_raw.data_ptr(), d_pk.data_ptr(), N, K, stream), "repack")
+    G.check(L.b200_gemv_bf16(t, d_pk.data_ptr(), d_xb.data_ptr(), d_y.data_ptr(), N, K, stream, 0), "gemv_bf16")
+    cuda.cuda.synchronize()
+    ref = O.gemv_q4_0_bf16(raw, N, K, xb) if t == G.Q4_0 else O.gemv(t, raw, N, K, x)
+    check_parity(d_y.cpu().numpy(), ref, f"{name} bf16")

@@ -1588,6 +1588,50 @@ int b200_bf16_to_f32(const uint16_t* src, float* dst, int64_t n, void* stream) {
     return launch_rc(bf16_to_f32_launch(src, dst, n, static_cast<cudaStream_t>(stream)), "b200_bf16_to_f32");
 }
 
+// F32 copy of a BF16 activation row, one growing buffer per (device, stream);
+// the conversion kernel and the GEMV that reads it are ordered on the stream.
+static float* bf16_staging(cudaStream_t stream, int64_t k) {
+    static std::mutex m;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<float*, int64_t>> bufs;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(m);
+    auto& b = bufs[{dev, stream}];
+    if (b.second < k) {
+        if (b.first) {
+            cudaStreamSynchronize(stream);
+            cudaFree(b.first);
+        }
+        b = {nullptr, 0};
+        const int64_t cap = std::max<int64_t>(k, 16384);
+        if (cudaMalloc(&b.first, static_cast<size_t>(cap) * sizeof(float)) != cudaSuccess) return nullptr;
+        b.second = cap;
+    }
+    return b.first;
+}
+
+int b200_gemv_bf16(int type, const void* w_packed, const uint16_t* x_bf16, float* y, int64_t n, int64_t k, void* stream,
+                   int pdl) {
+    const FormatInfo f = format_info(type);
+    if (!f.block_vals || k < 0 || k % f.block_vals || n < 0) {
+        set_error("b200_gemv_bf16: bad type %d / shape N=%ld K=%ld", type, long(n), long(k));
+        return -1;
+    }
+    if (n > 0 && (!w_packed || !x_bf16 || !y)) {
+        set_error("b200_gemv_bf16: null pointer");
+        return -1;
+    }
+    if (n == 0) return 0;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* xf = bf16_staging(st, k);
+    if (!xf) return launch_rc(cudaErrorMemoryAllocation, "b200_gemv_bf16 staging");
+    const int rc = launch_rc(bf16_to_f32_launch(x_bf16, xf, k, st), "b200_gemv_bf16 convert");
+    if (rc) return rc;
+    LaunchOpts lo;
+    lo.pdl = pdl != 0;
+    return launch_rc(gemv_launch(type, w_packed, xf, y, n, k, st, lo), "b200_gemv_bf16");
+}
+
 int b200_fill_normal(float* out, int64_t n, uint64_t seed, float sigma, void* stream) {
     return launch_rc(fill_normal_launch(out, n, seed, sigma, static_cast<cudaStream_t>(stream)), "b200_fill_normal");
 }

@@ -131,6 +131,7 @@ def lib() -> C.CDLL:
         "b200_repack": (C.c_int, [C.c_int, vp, vp, i64, i64, vp]),
         "b200_unpack": (C.c_int, [C.c_int, vp, vp, i64, i64, vp]),
         "b200_bf16_to_f32": (C.c_int, [vp, vp, i64, vp]),
+        "b200_gemv_bf16": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, vp, C.c_int]),
         "b200_fill_normal": (C.c_int, [vp, i64, C.c_uint64, C.c_float, vp]),
         "b200_quantize": (C.c_int, [C.c_int, vp, vp, i64, i64, vp]),
         "b200_repack_host": (C.c_int, [C.c_int, vp, vp, i64, i64]),
