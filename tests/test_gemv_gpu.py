@@ -404,3 +404,33 @@ def test_gemv_bf16_entry(cuda, G, O, name, N, K):
     cuda.cuda.synchronize()
     ref = O.gemv_q4_0_bf16(raw, N, K, xb) if t == G.Q4_0 else O.gemv(t, raw, N, K, x)
     check_parity(d_y.cpu().numpy(), ref, f"{name} bf16")
+
+
+def test_compute_graph_replays_repeated_device_lists(cuda, G, O):
+    """A node list seen again (all operands on the device) is captured into a
+    CUDA graph on its second call and replayed after that: new x contents at
+    the same addresses must give new, correct outputs, and a changed list
+    must run correctly too (eagerly, then captured again)."""
+    K = 1024
+    shapes = [(512, G.Q4_K), (256, G.Q6_K), (96, G.IQ4_XS)]  # MMA, MMA, stripe layout
+    raws = [O.quantize(t, normal_weights(N, K, seed=80 + i)) for i, (N, t) in enumerate(shapes)]
+    with G.Backend(0) as be:
+        buf = G.Buffer(sum(r.nbytes for r in raws) + 8 * 8192, dev=0)
+        ws = []
+        for (N, t), raw in zip(shapes, raws):
+            w = buf.alloc(G.tensor(t, [K, N, 1, 1]))
+            buf.set(w, _np_ptr(raw), 0, raw.nbytes)
+            ws.append(w)
+        d_x = cuda.empty(K, dtype=cuda.float32, device="cuda")
+        ys = [cuda.empty(N, dtype=cuda.float32, device="cuda") for N, _ in shapes]
+        xt = G.tensor(G.F32, [K, 1, 1, 1], data=d_x.data_ptr())
+        nodes = [G.mul_mat_node(ws[i], xt, ys[i].data_ptr(), shapes[i][0], name=f"g{i}") for i in range(3)]
+        for call in range(4):
+            x = normal_x(K, seed=90 + call)
+            d_x.copy_(cuda.from_numpy(x))
+            lst = nodes if call < 3 else nodes[:2]  # the fourth call changes the list
+            assert be.compute(lst), G.last_error()
+            be.synchronize()
+            for i in range(len(lst)):
+                check_parity(ys[i].cpu().numpy(), O.gemv(shapes[i][1], raws[i], shapes[i][0], K, x), f"call {call} node {i}")
+        buf.free()

@@ -321,6 +321,13 @@ struct Backend {
         uint32_t epoch = 0;
         int* err = nullptr;     // set by a gather kernel whose wait timed out
     } xg;
+    // CUDA graph of the last node list seen twice in a row with every operand
+    // on this device (see compute_graph); scratch_gen invalidates it when the
+    // x scratch it captured is reallocated.
+    std::vector<uint64_t> graph_sig;
+    bool graph_ok_sig = false;  // graph_sig was checked and is capturable
+    cudaGraphExec_t graph_exec = nullptr;
+    uint64_t graph_gen = 0, scratch_gen = 0;
 };
 
 // A scratch slot of at least xprep_bytes(N, K); growing it drains the stream first.
@@ -341,6 +348,7 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
             }
         }
         be->xscratch_bytes = cap;
+        ++be->scratch_gen;
     }
     void* p = be->xscratch[be->xscratch_next];
     be->xscratch_next ^= 1;
@@ -1026,6 +1034,49 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n) {
     return nccl_wait(be->comm, r, "grouped ncclAllGather");
 }
 
+// ------------------------------------------------------------- graph replay
+// The MUL_MAT fields that determine the launches of a node list.
+void graph_signature(ggml_tensor_xdna** nodes, size_t n, std::vector<uint64_t>* sig) {
+    sig->clear();
+    for (size_t i = 0; i < n; ++i) {
+        const ggml_tensor_xdna* t = nodes[i];
+        if (!t || t->op != GGML_OP_MUL_MAT) continue;
+        const ggml_tensor_xdna* a = t->src[0];
+        const ggml_tensor_xdna* b = t->src[1];
+        if (!a || !b) {
+            sig->push_back(~0ull);
+            continue;
+        }
+        const uint64_t v[] = {reinterpret_cast<uintptr_t>(a->data), uint64_t(a->type), uint64_t(a->ne[0]),
+                              uint64_t(a->ne[1]), uint64_t(a->ne[2]), uint64_t(a->ne[3]), a->nb[1],
+                              reinterpret_cast<uintptr_t>(b->data), uint64_t(b->type), uint64_t(b->ne[0]),
+                              uint64_t(b->ne[1]), uint64_t(b->ne[2]), b->nb[1], reinterpret_cast<uintptr_t>(t->data),
+                              uint64_t(t->ne[0]), uint64_t(t->ne[1]), t->nb[1]};
+        sig->insert(sig->end(), v, v + sizeof v / sizeof v[0]);
+    }
+}
+
+// Every MUL_MAT node runs on this device without host staging: resident
+// weights, device x and y, one activation row.
+bool device_only_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        const ggml_tensor_xdna* t = nodes[i];
+        if (!t || t->op != GGML_OP_MUL_MAT) continue;
+        const ggml_tensor_xdna* a = t->src[0];
+        const ggml_tensor_xdna* b = t->src[1];
+        if (!a || !b || b->ne[1] != 1 || b->ne[2] > 1 || b->ne[3] > 1 || a->ne[2] > 1 || a->ne[3] > 1) return false;
+        if (!resident_weights(a->data) || registry().find(a->data)->buft->dev != be->dev) return false;
+        if (!b->data || (reinterpret_cast<uintptr_t>(b->data) & 15u) || !is_device_pointer(b->data)) return false;
+        if (!t->data || !is_device_pointer(t->data)) return false;
+    }
+    return true;
+}
+
+void drop_graph(Backend* be) {
+    if (be->graph_exec) cudaGraphExecDestroy(be->graph_exec);
+    be->graph_exec = nullptr;
+}
+
 }  // namespace
 }  // namespace xb
 
@@ -1140,6 +1191,7 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         for (void* p : be->xscratch)
             if (p) cudaFree(p);
         release_exchange(be);
+        drop_graph(be);
         if (be->comm) nccl_api().CommDestroy(be->comm);
         cudaStreamDestroy(be->stream);
         be->magic = 0;
@@ -1170,12 +1222,7 @@ bool ggml_backend_xdna_supports_op(ggml_backend_t backend, const struct ggml_ten
     return supports_mul_mat(op);
 }
 
-bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_xdna** nodes, size_t n_nodes) {
-    if (!backend || !nodes || n_nodes == 0) return false;
-    Backend* be = as_backend(backend);
-    if (!be) return false;
-    std::lock_guard<std::mutex> lk(be->mtx);
-    DeviceGuard g(be->dev);
+static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
     static const bool trace = getenv("XDNA_TRACE_NODES") != nullptr;
     static const bool no_fuse = getenv("XDNA_NO_FUSE") != nullptr;
     bool ok = true;
@@ -1196,6 +1243,51 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
                     long(nodes[k]->src[0]->ne[1]), long(nodes[k]->src[0]->ne[0]), count > 1 ? " (fused)" : "");
         i += count;
     }
+    return ok;
+}
+
+// A node list that comes back unchanged (a decode step) is captured into a
+// CUDA graph on its second call and replayed from then on, when every operand
+// lives on this device and the backend drives one GPU (a sharded step's
+// exchange counts launches).  The first call runs eagerly, so the x scratch
+// the capture bakes in already has its final size.
+bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_xdna** nodes, size_t n_nodes) {
+    if (!backend || !nodes || n_nodes == 0) return false;
+    Backend* be = as_backend(backend);
+    if (!be) return false;
+    std::lock_guard<std::mutex> lk(be->mtx);
+    DeviceGuard g(be->dev);
+    static const bool no_graph = getenv("XDNA_B200_NO_GRAPH") != nullptr || getenv("XDNA_TRACE_NODES") != nullptr;
+    if (!no_graph && be->world == 1) {
+        std::vector<uint64_t> sig;
+        graph_signature(nodes, n_nodes, &sig);
+        if (sig == be->graph_sig && be->graph_ok_sig) {
+            if (be->graph_exec && be->graph_gen != be->scratch_gen) drop_graph(be);
+            if (!be->graph_exec) {
+                cudaGraph_t graph = nullptr;
+                bool cap = cudaStreamBeginCapture(be->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+                const bool ran = cap && run_nodes(be, nodes, n_nodes);
+                cap = cudaStreamEndCapture(be->stream, &graph) == cudaSuccess && cap;
+                if (ran && cap && graph && cudaGraphInstantiate(&be->graph_exec, graph, 0) == cudaSuccess) {
+                    be->graph_gen = be->scratch_gen;
+                } else {
+                    be->graph_exec = nullptr;
+                    be->graph_ok_sig = false;  // run this list eagerly from now on
+                }
+                if (graph) cudaGraphDestroy(graph);
+                cudaGetLastError();
+            }
+            if (be->graph_exec) {
+                const bool ok = cuda_ok(cudaGraphLaunch(be->graph_exec, be->stream), "graph launch");
+                return flush(be) && ok;
+            }
+        } else if (sig != be->graph_sig) {
+            drop_graph(be);
+            be->graph_sig.swap(sig);
+            be->graph_ok_sig = device_only_nodes(be, nodes, n_nodes);
+        }
+    }
+    const bool ok = run_nodes(be, nodes, n_nodes);
     const bool flushed = flush(be);
     return ok && flushed;
 }
