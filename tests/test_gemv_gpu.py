@@ -237,11 +237,12 @@ def test_compute_graph_rejects_bad_nodes(cuda, G):
         assert not be.compute([G.mul_mat_node(w, x, _np_ptr(y_data), N)])
 
 
-def test_buffer_roundtrip_and_partial_writes(cuda, G, O):
+@pytest.mark.parametrize("N", [37, 64])  # stripe tiles; the MMA layout (N % 16 == 0)
+def test_buffer_roundtrip_and_partial_writes(cuda, G, O, N):
     rng = np.random.default_rng(9)
     for name in TYPES:
         t = G.CLAIMED[name]
-        N, K = 37, 512
+        K = 512
         raw = random_blocks(t, N, K, seed=11)
         buf = G.Buffer(2 * raw.nbytes + 8192, dev=0)
         wt = buf.alloc(G.tensor(t, [K, N, 1, 1]))
@@ -265,9 +266,10 @@ def test_buffer_roundtrip_and_partial_writes(cuda, G, O):
         raw2[100:800] = 0x5A
         buf.get(wt, _np_ptr(back), 0, raw.nbytes)
         assert np.array_equal(back, raw2), name
-        buf.clear(0x33)
-        buf.get(wt, _np_ptr(back), 0, raw.nbytes)
-        assert np.all(back == 0x33), name
+        for v in (0x00, 0x5A):  # 0x5A: unequal nibbles and bit pairs
+            buf.clear(v)
+            buf.get(wt, _np_ptr(back), 0, raw.nbytes)
+            assert np.all(back == v), (name, v)
         buf.free()
 
 

@@ -1560,13 +1560,16 @@ bool ggml_backend_xdna_buffer_clear(ggml_backend_buffer_t buffer, uint8_t value)
     }
     DeviceGuard g(b->buft->dev);
     if (b->size && !cuda_ok(cudaMemset(b->base, value, b->size), "clear")) return false;
-    // Every byte of the GGUF view is now `value`; stripe tiles whose repack
-    // transposes bit planes (Q5_K qh, Q3_K hmask) need the transposed value.
+    // Every byte of the GGUF view is now `value`.  Every kernel layout is a
+    // permutation of the GGUF bits, so 0x00 and 0xFF read back unchanged; any
+    // other value reads back permuted (nibbles re-paired, bit planes
+    // transposed), so packed tensors are rewritten through the repack.
+    if (value == 0x00 || value == 0xFF) return true;
     std::vector<std::pair<uintptr_t, TensorInfo>> fix;
     {
         std::lock_guard<std::mutex> lk(b->mtx);
         for (auto& kv : b->tensors)
-            if (kv.second.packed && (kv.second.type == T_Q5_K || kv.second.type == T_Q3_K)) fix.push_back(kv);
+            if (kv.second.packed) fix.push_back(kv);
     }
     if (fix.empty()) return true;
     Staging& st = staging_for(b->buft->dev);

@@ -374,22 +374,39 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //   [1536, 1664) per lane 4 B: low nibbles of its 8 scales, [1664, 1728) per
 //                lane 2 B: their high pairs (scale order as Q6_K's int8 scales);
 //   [1728, 1760) the 16 rows' fp16 d.
+//
+// IQ4_XS (4-bit indices into the 16 IQ4_NL values, 6-bit scales per 32):
+//   [0, 2048)    per lane and chunk pair 16 B; word 2 (c % 2) holds the
+//                indices of A registers a0 (bits 0-15) and a1 (bits 16-31) of
+//                chunk c, word 2 (c % 2) + 1 those of a2 / a3, one 4-bit index
+//                per value in value order (byte_perm selector form);
+//   [2048, 2176) the 16 rows' first 8 block bytes {d, scales_h, scales_l[4]}.
 XB_HD int mma_group_bytes(int type) {
-    return type == T_Q5_K ? 2816 : (type == T_Q6_K ? 3360 : (type == T_Q3_K ? 1760 : MMA_GROUP_BYTES));
+    return type == T_Q5_K ? 2816
+                          : (type == T_Q6_K ? 3360
+                                            : (type == T_Q3_K ? 1760 : (type == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
 }
 XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : (type == T_Q6_K ? 3072 : 2048); }
 // GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
 XB_HD int mma_row_group_bytes(int type) {
-    return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : (type == T_Q3_K ? 110 : 144));
+    return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : (type == T_Q3_K ? 110 : (type == T_IQ4_XS ? 136 : 144)));
 }
 // x blocks (B columns) of 16 values instead of 32
 XB_HD bool mma_blk16(int type) { return type == T_Q6_K || type == T_Q3_K; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
-    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q3_K) && N > 0 &&
-            K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0)
+    return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q3_K ||
+             type == T_IQ4_XS) &&
+            N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0)
                ? 1
                : 0;
+}
+
+// IQ4_XS index of value v: qs[16 ib + j % 16] nibble j / 16 of sub-block ib = v / 32
+XB_HD const uint8_t* iq4_idx(const uint8_t* row, int64_t gi, int v, int* shift) {
+    const int ib = v >> 5, j = v & 31;
+    *shift = 4 * (j >> 4);
+    return row + gi * 136 + 8 + 16 * ib + (j & 15);
 }
 
 // Q3_K: low pair / high bit of value v, and the 6-bit scale i of a row's group
@@ -469,6 +486,27 @@ XB_HD int q5_plane_bit(int c, int k, int j) { return 8 * j + ((c & 1) ? 0 : 4) +
 // One group (gi) of one 16-row tile: GGUF rows (tile row 0 at `raw`, stride
 // row_bytes) -> MMA layout at `out` (2304 bytes), or the inverse.
 XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64_t gi, uint8_t* out) {
+    if (type == T_IQ4_XS) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c)
+                for (int half = 0; half < 2; ++half) {  // word: registers (a0, a1) or (a2, a3)
+                    uint32_t w = 0;
+                    for (int k2 = 0; k2 < 2; ++k2) {
+                        const int k = 2 * half + k2;  // a0 row g / a1 row g+8 of column t, a2 / a3 of t + 4
+                        const uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                        for (int j = 0; j < 4; ++j) {
+                            int sh;
+                            const uint8_t* p = iq4_idx(row, gi, mma_value(type, c, t, k >> 1, j), &sh);
+                            w |= static_cast<uint32_t>((*p >> sh) & 0xFu) << (16 * k2 + 4 * j);
+                        }
+                    }
+                    put32(out + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * half, w);
+                }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(out + 2048 + 8 * r, raw + r * row_bytes + gi * 136, 8);
+        return;
+    }
     if (type == T_Q3_K) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;
@@ -583,6 +621,27 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 }
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
+    if (type == T_IQ4_XS) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c)
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t w = get32(in + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * half);
+                    for (int k2 = 0; k2 < 2; ++k2) {
+                        const int k = 2 * half + k2;
+                        uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                        for (int j = 0; j < 4; ++j) {
+                            int sh;
+                            uint8_t* p = const_cast<uint8_t*>(iq4_idx(row, gi, mma_value(type, c, t, k >> 1, j), &sh));
+                            const uint32_t q = (w >> (16 * k2 + 4 * j)) & 0xFu;
+                            *p = uint8_t((*p & ~(0xFu << sh)) | (q << sh));
+                        }
+                    }
+                }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 136, in + 2048 + 8 * r, 8);
+        return;
+    }
     if (type == T_Q3_K) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;

@@ -34,6 +34,7 @@
 
 #include "formats.cuh"
 #include "gemv.cuh"
+#include "iq_tables.h"  // generated at build time from the gguf package
 
 namespace xb {
 namespace {
@@ -47,6 +48,14 @@ __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
 }
 __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
+}
+
+__device__ __forceinline__ void mma_s8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -235,7 +244,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 // bytes of one (16-row tile, 256-value group) unit of format TYPE
 template <int TYPE>
 constexpr int kUnitBytes =
-    TYPE == T_Q5_K ? 2816 : (TYPE == T_Q6_K ? 3360 : (TYPE == T_Q3_K ? 1760 : MMA_GROUP_BYTES));
+    TYPE == T_Q5_K ? 2816
+                   : (TYPE == T_Q6_K ? 3360 : (TYPE == T_Q3_K ? 1760 : (TYPE == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
 template <int TYPE>
 constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
 template <int TYPE>
@@ -379,18 +389,73 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
     }
 }
 
+// IQ4_XS: value = d * (ls - 32) * kvalues[q] with a 6-bit ls per 32 values
+// (ggml-quants.c dequantize_row_iq4_xs).  A = kvalues[q] as s8, looked up with
+// byte_perm from the 16-entry table held in four registers: the low three bits
+// of each index pick a byte from entries 0-7 and from 8-15, bit 3 picks which.
+// Each index word holds registers (k, k+1) as 16-bit selector halves.
+__device__ __forceinline__ void iq4nl_lookup2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    constexpr uint32_t k0 = XB_IQ4NL_U8_0 ^ 0x80808080u, k1 = XB_IQ4NL_U8_1 ^ 0x80808080u;  // kvalues as s8
+    constexpr uint32_t k2 = XB_IQ4NL_U8_2 ^ 0x80808080u, k3 = XB_IQ4NL_U8_3 ^ 0x80808080u;
+    const uint32_t s = w & 0x77777777u;
+    const uint32_t pick = ((w >> 1) & 0x44444444u) | 0x32103210u;
+    lo = __byte_perm(__byte_perm(k0, k1, s), __byte_perm(k2, k3, s), pick);
+    const uint32_t s16 = s >> 16;
+    hi = __byte_perm(__byte_perm(k0, k1, s16), __byte_perm(k2, k3, s16), pick >> 16);
+}
+
+__device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t* fb, int fc,
+                                                const float* __restrict__ sc_, int lane, int g, int t, float& y0,
+                                                float& y8) {
+    uint4 A[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
+    const uint2 h0 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + g);  // {d | scales_h << 16, scales_l}
+    const uint2 h8 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + g + 8);
+    int C[3][4];
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        uint32_t a0, a1, a2, a3;
+        iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1)), a0, a1);
+        iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1) + 1), a2, a3);
+        mma_s8s8(C[0], a0, a1, a2, a3, q.x, q.y);
+        mma_s8s8(C[1], a0, a1, a2, a3, q.z, q.w);
+        mma_s8s8(C[2], a0, a1, a2, a3, r.x, r.y);
+    }
+    // |sum| <= 32 * 127 * 2^23 passes 2^31: join the planes in F32
+    float T[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
+    // six-bit scales of sub-blocks 2t, 2t+1: low nibbles at bit 4 ib of
+    // scales_l, high pairs at bit 2 ib of scales_h
+    float k6[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint2 hh = h ? h8 : h0;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            const int ib = 2 * t + b;
+            const uint32_t ls = ((hh.y >> (4 * ib)) & 0xFu) | (((hh.x >> (16 + 2 * ib)) & 3u) << 4);
+            k6[h][b] = static_cast<float>(static_cast<int>(ls) - 32);
+        }
+    }
+    y0 = fmaf(h2f(h0.x), fmaf(k6[0][0] * sc2.x, T[0], k6[0][1] * sc2.y * T[1]), y0);
+    y8 = fmaf(h2f(h8.x), fmaf(k6[1][0] * sc2.x, T[2], k6[1][1] * sc2.y * T[3]), y8);
+}
+
+// Q4_0, Q4_K, Q5_K: one set of 8 thirty-two-value blocks, 4- or 5-bit q.
 template <int TYPE>
-__device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
-                                          const float* __restrict__ xs_, int lane, int g, int t, float& y0,
-                                          float& y8) {
-    if constexpr (TYPE == T_Q6_K) {
-        group_dot_q6k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
-        return;
-    }
-    if constexpr (TYPE == T_Q3_K) {
-        group_dot_q3k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
-        return;
-    }
+__device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* fb, int fc,
+                                              const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
+                                              int g, int t, float& y0, float& y8) {
     uint4 A[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
@@ -482,6 +547,20 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         y0 = fmaf(dg0, fmaf(s0, T[0], -8.0f * x0), fmaf(dg1, fmaf(s1, T[1], -8.0f * x1), y0));
         y8 = fmaf(d80, fmaf(s0, T[2], -8.0f * x0), fmaf(d81, fmaf(s1, T[3], -8.0f * x1), y8));
     }
+}
+
+template <int TYPE>
+__device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
+                                          const float* __restrict__ xs_, int lane, int g, int t, float& y0,
+                                          float& y8) {
+    if constexpr (TYPE == T_Q6_K)
+        group_dot_q6k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+    else if constexpr (TYPE == T_Q3_K)
+        group_dot_q3k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+    else if constexpr (TYPE == T_IQ4_XS)
+        group_dot_iq4xs(gb, fb, fc, sc_, lane, g, t, y0, y8);
+    else
+        group_dot_nib<TYPE>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
 
 template <int TYPE>
@@ -820,7 +899,7 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
-    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K) {
+    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K || type == T_IQ4_XS) {
         const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
         if (pack)
             mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
@@ -848,8 +927,9 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
-    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K) || nseg < 1 ||
-        nseg > kMaxSegs)
+    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K &&
+         type != T_IQ4_XS) ||
+        nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
         return cudaErrorInvalidValue;
@@ -934,6 +1014,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     if (type == T_Q5_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q5_K>, a);
     if (type == T_Q6_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q6_K>, a);
     if (type == T_Q3_K) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q3_K>, a);
+    if (type == T_IQ4_XS) return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ4_XS>, a);
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
