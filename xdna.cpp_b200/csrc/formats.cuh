@@ -376,10 +376,12 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //   [1728, 1760) the 16 rows' fp16 d.
 //
 // IQ4_XS (4-bit indices into the 16 IQ4_NL values, 6-bit scales per 32):
-//   [0, 2048)    per lane and chunk pair 16 B; word 2 (c % 2) holds the
-//                indices of A registers a0 (bits 0-15) and a1 (bits 16-31) of
-//                chunk c, word 2 (c % 2) + 1 those of a2 / a3, one 4-bit index
-//                per value in value order (byte_perm selector form);
+//   [0, 2048)    per lane and chunk pair 16 B; word 2 (c % 2) holds the codes
+//                of A registers a0 (bits 0-15) and a1 (bits 16-31) of chunk c,
+//                word 2 (c % 2) + 1 those of a2 / a3, one 4-bit code per value
+//                in value order (byte_perm selector form).  code = the index
+//                with bits 2 and 3 swapped (iq4_code), which pairs codes i and
+//                i + 8 on values of one sign for the two-table decode;
 //   [2048, 2176) the 16 rows' first 8 block bytes {d, scales_h, scales_l[4]}.
 XB_HD int mma_group_bytes(int type) {
     return type == T_Q5_K ? 2816
@@ -402,6 +404,8 @@ XB_HD int layout_kind(int type, int64_t N, int64_t K) {
                : 0;
 }
 
+// IQ4_XS layout code of an index (an involution: also the index of a code)
+XB_HD uint32_t iq4_code(uint32_t q) { return (q & 3u) | (((q >> 3) & 1u) << 2) | (((q >> 2) & 1u) << 3); }
 // IQ4_XS index of value v: qs[16 ib + j % 16] nibble j / 16 of sub-block ib = v / 32
 XB_HD const uint8_t* iq4_idx(const uint8_t* row, int64_t gi, int v, int* shift) {
     const int ib = v >> 5, j = v & 31;
@@ -498,7 +502,7 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
                         for (int j = 0; j < 4; ++j) {
                             int sh;
                             const uint8_t* p = iq4_idx(row, gi, mma_value(type, c, t, k >> 1, j), &sh);
-                            w |= static_cast<uint32_t>((*p >> sh) & 0xFu) << (16 * k2 + 4 * j);
+                            w |= iq4_code((*p >> sh) & 0xFu) << (16 * k2 + 4 * j);
                         }
                     }
                     put32(out + ((c >> 1) * 32 + lane) * 16 + 8 * (c & 1) + 4 * half, w);
@@ -633,7 +637,7 @@ XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int6
                         for (int j = 0; j < 4; ++j) {
                             int sh;
                             uint8_t* p = const_cast<uint8_t*>(iq4_idx(row, gi, mma_value(type, c, t, k >> 1, j), &sh));
-                            const uint32_t q = (w >> (16 * k2 + 4 * j)) & 0xFu;
+                            const uint32_t q = iq4_code((w >> (16 * k2 + 4 * j)) & 0xFu);
                             *p = uint8_t((*p & ~(0xFu << sh)) | (q << sh));
                         }
                     }

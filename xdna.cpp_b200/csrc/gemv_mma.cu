@@ -1,4 +1,4 @@
-// Integer tensor-core GEMV for the linear formats (Q4_0, Q3_K, Q4_K, Q5_K, Q6_K) on sm_100a.
+// Integer tensor-core GEMV for Q4_0, Q3_K, Q4_K, Q5_K, Q6_K and IQ4_XS on sm_100a.
 //
 // Why tensor cores for an M = 1 GEMV: the contraction is bandwidth bound, but
 // unpacking and multiplying 4-bit weights on the FP32 pipes costs ~4
@@ -98,9 +98,13 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //   count   one arrival counter per tile (zeroed by xprep_kernel)
 //   partial kMaxCtas CTAs * 2 slots * 16 floats (level-2 CTA sums)
 // ---------------------------------------------------------------------------
-constexpr int kWarps = 8;
+// One CTA of 24 warps per SM: warps of one CTA are scheduled as equals,
+// while of three 8-warp CTAs on an SM the one that started first finished
+// about 2.5 us (10 %) before the last, leaving the SM short of loads in flight
+// at the end of every launch.
+constexpr int kWarps = 24;
 constexpr int kGemvThreads = kWarps * 32;
-constexpr int kCtasPerSm = 3;
+constexpr int kCtasPerSm = 1;
 constexpr int kMaxCtas = 512;        // bounds the partial-slot area
 constexpr int kPrefetch = 4;         // groups ahead per warp (bulk L2 prefetch)
 constexpr int kSlotBytes = 32;
@@ -390,18 +394,24 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
 }
 
 // IQ4_XS: value = d * (ls - 32) * kvalues[q] with a 6-bit ls per 32 values
-// (ggml-quants.c dequantize_row_iq4_xs).  A = kvalues[q] as s8, looked up with
-// byte_perm from the 16-entry table held in four registers: the low three bits
-// of each index pick a byte from entries 0-7 and from 8-15, bit 3 picks which.
-// Each index word holds registers (k, k+1) as 16-bit selector halves.
+// (ggml-quants.c dequantize_row_iq4_xs).  A = kvalues[q] as s8 from two
+// 8-entry byte tables held in registers.  The layout stores code = q with bits
+// 2 and 3 swapped, so codes i and i + 8 name values of one sign.  prmt with a
+// selector nibble below 8 copies byte i; with bit 3 set it replicates the sign
+// of byte i.  XA holds the values of codes 0-7 and XB those of codes 8-15
+// (complemented where the pair is negative); so for a code below 8 the XB
+// lookup (code ^ 8) gives 0, for a code of 8 or more the XA lookup gives the
+// pair's sign, and the XOR of the two lookups is the value either way.
+// Each code word holds registers (k, k+1) as 16-bit selector halves.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
 __device__ __forceinline__ void iq4nl_lookup2(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    constexpr uint32_t k0 = XB_IQ4NL_U8_0 ^ 0x80808080u, k1 = XB_IQ4NL_U8_1 ^ 0x80808080u;  // kvalues as s8
-    constexpr uint32_t k2 = XB_IQ4NL_U8_2 ^ 0x80808080u, k3 = XB_IQ4NL_U8_3 ^ 0x80808080u;
-    const uint32_t s = w & 0x77777777u;
-    const uint32_t pick = ((w >> 1) & 0x44444444u) | 0x32103210u;
-    lo = __byte_perm(__byte_perm(k0, k1, s), __byte_perm(k2, k3, s), pick);
-    const uint32_t s16 = s >> 16;
-    hi = __byte_perm(__byte_perm(k0, k1, s16), __byte_perm(k2, k3, s16), pick >> 16);
+    const uint32_t x = w ^ 0x88888888u;
+    lo = prmt(XB_IQ4NL_XA_0, XB_IQ4NL_XA_1, w) ^ prmt(XB_IQ4NL_XB_0, XB_IQ4NL_XB_1, x);
+    hi = prmt(XB_IQ4NL_XA_0, XB_IQ4NL_XA_1, w >> 16) ^ prmt(XB_IQ4NL_XB_0, XB_IQ4NL_XB_1, x >> 16);
 }
 
 __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t* fb, int fc,
