@@ -9,6 +9,7 @@ model shapes, K validation, concurrency) and tests/test-kquants-gemv.cpp
 (per-type accuracy, zero invariance, shape sweep).
 """
 import ctypes as C
+import os
 import threading
 
 import numpy as np
@@ -355,6 +356,78 @@ def test_compute_graph_fuses_nodes_sharing_x(cuda, G, O):
                 check_parity(got[i], O.gemv(shapes[i][1], raws[i], shapes[i][0], K, x), f"fused node {i} rep {rep}")
             check_parity(got[3], O.gemv(G.Q4_K, raws[3], shapes[3][0], K, got[0]), f"consumer rep {rep}")
         buf.free()
+
+
+# A decode-style chain of MMA launches, each reading an output of the one
+# before: (output, type, N, input).  K of a node = N of its input; "h0" is the
+# chain's input (K = 1024).  a0/a1/a2 and c0/c1 share x (fused launches); the
+# Q6_K and Q3_K consumers take 16-value x blocks.
+CHAIN = [("a0", "Q4_K", 1024, "h0"), ("a1", "Q4_K", 256, "h0"), ("a2", "Q4_K", 256, "h0"),
+         ("b", "IQ4_XS", 512, "a0"), ("c0", "Q5_K", 768, "b"), ("c1", "Q5_K", 768, "b"),
+         ("d", "Q6_K", 512, "c0"), ("e", "Q3_K", 256, "d"), ("f", "Q4_0", 512, "e")]
+
+
+def run_chain(cuda, G, O, one_call: bool):
+    """Runs CHAIN through compute_graph (one call for the whole chain, or one
+    call per node, where no launch can prepare the next one's x) and returns
+    the raw weights and the outputs of every node."""
+    dims = {"h0": 1024}
+    for out, _, N, _ in CHAIN:
+        dims[out] = N
+    raws = {out: O.quantize(G.CLAIMED[t], normal_weights(N, dims[src], seed=300 + i), nthreads=4)
+            for i, (out, t, N, src) in enumerate(CHAIN)}
+    with G.Backend(0) as be:
+        buf = G.Buffer(sum(r.nbytes for r in raws.values()) + 16 * 8192, dev=0)
+        acts = {"h0": to_dev(cuda, normal_x(1024, seed=299))}
+        for out, _, N, _ in CHAIN:
+            acts[out] = cuda.full((N,), float("nan"), dtype=cuda.float32, device="cuda")
+        nodes = []
+        for out, t, N, src in CHAIN:
+            w = buf.alloc(G.tensor(G.CLAIMED[t], [dims[src], N, 1, 1]))
+            buf.set(w, _np_ptr(raws[out]), 0, raws[out].nbytes)
+            xt = G.tensor(G.F32, [dims[src], 1, 1, 1], data=acts[src].data_ptr())
+            nodes.append(G.mul_mat_node(w, xt, acts[out].data_ptr(), N, name=out))
+        if one_call:
+            assert be.compute(nodes), G.last_error()
+        else:
+            for n in nodes:
+                assert be.compute([n]), G.last_error()
+        be.synchronize()
+        got = {k: v.cpu().numpy() for k, v in acts.items()}
+        buf.free()
+    return raws, got
+
+
+def test_compute_graph_chain_prepares_next_x(cuda, G, O):
+    """Within one compute_graph call a launch whose output is the next
+    launch's x prepares that x in its epilogue (no x-preparation kernel): the
+    results are bit-identical to one call per node, and every node matches the
+    oracle on its actual input."""
+    raws, chained = run_chain(cuda, G, O, one_call=True)
+    _, single = run_chain(cuda, G, O, one_call=False)
+    for out, t, N, src in CHAIN:
+        np.testing.assert_array_equal(chained[out], single[out], err_msg=out)
+        check_parity(chained[out], O.gemv(G.CLAIMED[t], raws[out], N, chained[src].size, chained[src]), out)
+
+
+def test_compute_graph_chain_trace_shows_prepared_x(cuda):
+    """The node trace (XDNA_TRACE_NODES) of the chain: every launch after the
+    first reads an x prepared by the launch before it."""
+    import subprocess
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    code = ("import sys; sys.path[:0] = [%r, %r, %r]; import torch, ggml_b200 as G, oracle as O; "
+            "import test_gemv_gpu as T; T.run_chain(torch, G, O, True)"
+            % (here, os.path.join(here, "..", "xdna.cpp_b200"), os.path.join(here, "..", "oracle")))
+    env = dict(os.environ, XDNA_TRACE_NODES="1")
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stderr.splitlines() if "[b200 trace]" in ln]
+    assert len(lines) == len(CHAIN), r.stderr[-2000:]
+    ready = [ln for ln in lines if "x from the previous launch" in ln]
+    # launches: (a0 a1 a2) b (c0 c1) d e f -> 6, all but the first read a prepared x
+    assert len(ready) == 1 + 2 + 1 + 1 + 1, "\n".join(lines)
 
 
 @pytest.mark.parametrize("name", ["Q4_K", "Q6_K", "Q4_0"])

@@ -333,10 +333,11 @@ struct Backend {
 // A scratch slot of at least xprep_bytes(N, K); growing it drains the stream first.
 void* backend_xscratch(Backend* be, int64_t N, int64_t K);
 
-void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
-    const size_t need = xprep_bytes(N, K);
+// Both x-scratch slots hold at least `need` bytes (growing them waits for
+// the stream: never inside a stream capture).
+bool backend_xscratch_reserve(Backend* be, size_t need) {
     if (need > be->xscratch_bytes) {
-        if (cudaStreamSynchronize(be->stream) != cudaSuccess) return nullptr;
+        if (cudaStreamSynchronize(be->stream) != cudaSuccess) return false;
         const size_t cap = std::max<size_t>(need, 1u << 20);
         for (int s = 0; s < 2; ++s) {
             if (be->xscratch[s]) cudaFree(be->xscratch[s]);
@@ -344,12 +345,17 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
             if (!cuda_ok(cudaMalloc(&be->xscratch[s], cap), "x scratch alloc") ||
                 !cuda_ok(cudaMemset(be->xscratch[s], 0, cap), "x scratch clear")) {
                 be->xscratch_bytes = 0;
-                return nullptr;
+                return false;
             }
         }
         be->xscratch_bytes = cap;
         ++be->scratch_gen;
     }
+    return true;
+}
+
+void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
+    if (!backend_xscratch_reserve(be, xprep_bytes(N, K))) return nullptr;
     void* p = be->xscratch[be->xscratch_next];
     be->xscratch_next ^= 1;
     return p;
@@ -753,7 +759,15 @@ bool all_gather_rows(Backend* be, float* y_full, int64_t n_local) {
 }
 
 // One MUL_MAT node -> jobs (reference process_mul_mat_node, :149-308).
-bool run_node(Backend* be, ggml_tensor_xdna* node) {
+// A planned MMA launch (compute_graph): its scratch slot, and whether it
+// prepares the next launch's x (feed) or runs on x prepared by the previous one.
+struct MmaPlan {
+    void* scratch = nullptr;
+    const MmaFeed* feed = nullptr;
+    bool x_ready = false;
+};
+
+bool run_node(Backend* be, ggml_tensor_xdna* node, const MmaPlan* plan = nullptr) {
     ggml_tensor_xdna* src0 = node->src[0];
     ggml_tensor_xdna* src1 = node->src[1];
     const char* name = node->name;
@@ -885,8 +899,12 @@ bool run_node(Backend* be, ggml_tensor_xdna* node) {
                 LaunchOpts lo;
                 lo.pdl = true;  // kernels wait (griddepcontrol) before touching what earlier work writes
                 if (layout_kind(src0->type, N, K) == 1) {
-                    lo.scratch = backend_xscratch(be, N, K);
+                    lo.scratch = plan && plan->scratch ? plan->scratch : backend_xscratch(be, N, K);
                     if (!lo.scratch) return false;
+                    if (plan) {
+                        lo.feed = plan->feed;
+                        lo.x_ready = plan->x_ready;
+                    }
                 }
                 float* y_local = sharded ? yd + be->rank * N : yd;
                 if (!cuda_ok(gemv_launch(src0->type, w_dev, xd, y_local, N, K, be->stream, lo), "gemv launch"))
@@ -973,14 +991,14 @@ size_t fused_run_length(Backend* be, ggml_tensor_xdna** nodes, size_t i, size_t 
     return n;
 }
 
-bool run_fused(Backend* be, const FusableNode* f, size_t n) {
+bool run_fused(Backend* be, const FusableNode* f, size_t n, const MmaPlan* plan = nullptr) {
     MmaSegment segs[MMA_MAX_SEGMENTS];
     int64_t rows = 0;
     for (size_t k = 0; k < n; ++k) {
         segs[k] = f[k].seg;
         rows += f[k].seg.N;
     }
-    void* scratch = backend_xscratch(be, rows, f[0].K);
+    void* scratch = plan && plan->scratch ? plan->scratch : backend_xscratch(be, rows, f[0].K);
     if (!scratch) return false;
     // row-sharded: rows travel to the peers from the GEMV itself when the
     // outputs fit the exchange buffers; NCCL all-gather otherwise
@@ -1016,7 +1034,8 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n) {
                                           gs, static_cast<int>(n), xg.err, be->stream),
                        "exchange gather launch");
     }
-    if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true),
+    if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true,
+                                       nullptr, plan ? plan->feed : nullptr, plan && plan->x_ready),
                  "fused gemv launch"))
         return false;
     bool any = false;
@@ -1225,23 +1244,76 @@ bool ggml_backend_xdna_supports_op(ggml_backend_t backend, const struct ggml_ten
 static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
     static const bool trace = getenv("XDNA_TRACE_NODES") != nullptr;
     static const bool no_fuse = getenv("XDNA_NO_FUSE") != nullptr;
-    bool ok = true;
-    for (size_t i = 0; i < n_nodes && ok;) {
+    // Plan the launches first.  Device-resident MMA launches (one fused run
+    // or one node) get their scratch slots in order, alternating; where a
+    // launch's x is, in full, one output segment of the launch before it, that
+    // launch's epilogue prepares the x (MmaFeed) and the x-preparation kernel
+    // is left out.
+    struct Run {
+        size_t i, count, nf;
+        int64_t rows;  // of all the launch's segments
+        bool fused, planned;
+        FusableNode f[MMA_MAX_SEGMENTS];
+        MmaPlan plan;
+        MmaFeed feed;
+    };
+    static thread_local std::vector<Run> runs;  // reused: no allocation per call
+    runs.clear();
+    size_t need = 0;
+    for (size_t i = 0; i < n_nodes;) {
         ggml_tensor_xdna* node = nodes[i];
         if (!node || node->op != GGML_OP_MUL_MAT) {
             ++i;
             continue;
         }
-        FusableNode f[MMA_MAX_SEGMENTS];
-        const size_t run = no_fuse ? 0 : fused_run_length(be, nodes, i, n_nodes, f);
-        const size_t count = run > 1 ? run : 1;
-        const bool fused = run > 1 || (run == 1 && f[0].sharded && be->xg.ok);
-        ok = fused ? run_fused(be, f, run) : run_node(be, node);
-        for (size_t k = i; trace && ok && k < i + count; ++k)
-            fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued%s\n", k,
-                    nodes[k]->name[0] ? nodes[k]->name : "unnamed", nodes[k]->src[0]->type,
-                    long(nodes[k]->src[0]->ne[1]), long(nodes[k]->src[0]->ne[0]), count > 1 ? " (fused)" : "");
-        i += count;
+        Run r;
+        r.i = i;
+        r.nf = no_fuse ? (fusable(be, node, &r.f[0]) ? 1 : 0) : fused_run_length(be, nodes, i, n_nodes, r.f);
+        r.count = !no_fuse && r.nf > 1 ? r.nf : 1;
+        r.fused = !no_fuse && (r.nf > 1 || (r.nf == 1 && r.f[0].sharded && be->xg.ok));
+        r.planned = r.nf > 0;
+        const size_t nseg = r.fused ? r.nf : 1;
+        int64_t rows = 0;
+        for (size_t j = 0; j < nseg && r.planned; ++j) {
+            r.planned = !r.f[j].sharded;
+            rows += r.f[j].seg.N;
+        }
+        r.rows = rows;
+        if (r.planned) need = std::max(need, xprep_bytes(rows, r.f[0].K));
+        runs.push_back(r);
+        i += r.count;
+    }
+    if (need > 0 && !backend_xscratch_reserve(be, need)) return false;
+    for (Run& r : runs)
+        if (r.planned) {
+            r.plan.scratch = be->xscratch[be->xscratch_next];
+            be->xscratch_next ^= 1;
+        }
+    for (size_t k = 0; k + 1 < runs.size(); ++k) {
+        Run &r = runs[k], &q = runs[k + 1];
+        if (!r.planned || !q.planned || r.plan.scratch == q.plan.scratch) continue;
+        const size_t nseg = r.fused ? r.nf : 1;
+        for (size_t j = 0; j < nseg; ++j)
+            if (r.f[j].seg.y == q.f[0].x && r.f[j].seg.N == q.f[0].K) {
+                r.feed.next_scratch = q.plan.scratch;
+                r.feed.next_rows = q.rows;
+                r.feed.seg = static_cast<int>(j);
+                r.feed.bl = mma_blk16(q.f[0].type) ? 16 : 32;
+                r.plan.feed = &r.feed;
+                q.plan.x_ready = true;
+                break;
+            }
+    }
+    bool ok = true;
+    for (size_t k = 0; k < runs.size() && ok; ++k) {
+        const Run& r = runs[k];
+        const MmaPlan* mp = r.planned ? &r.plan : nullptr;
+        ok = r.fused ? run_fused(be, r.f, r.nf, mp) : run_node(be, nodes[r.i], mp);
+        for (size_t j = r.i; trace && ok && j < r.i + r.count; ++j)
+            fprintf(stderr, "[b200 trace] node %3zu: %-30s | type=%2d | N=%6ld K=%5ld | queued%s%s%s\n", j,
+                    nodes[j]->name[0] ? nodes[j]->name : "unnamed", nodes[j]->src[0]->type,
+                    long(nodes[j]->src[0]->ne[1]), long(nodes[j]->src[0]->ne[0]), r.count > 1 ? " (fused)" : "",
+                    r.plan.x_ready ? " (x from the previous launch)" : "", r.plan.feed ? " (prepares the next x)" : "");
     }
     return ok;
 }

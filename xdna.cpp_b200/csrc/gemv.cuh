@@ -6,9 +6,24 @@
 
 namespace xb {
 
+// A launch whose output segment `seg` is, in full, the x of the launch that
+// follows it on the stream: its epilogue writes that x's digit fragments,
+// scales and sums into the next launch's scratch (next_scratch, sized by
+// xprep_bytes for the next launch) and clears that launch's counters, and the
+// next launch runs with x_ready set (no x-preparation kernel).  bl = the next launch's x block: 32, or 16 for
+// the types with 16-value sub-blocks.
+struct MmaFeed {
+    void* next_scratch = nullptr;
+    int64_t next_rows = 0;  // rows of the next launch (all its segments): the counters it needs cleared
+    int seg = 0;
+    int bl = 32;
+};
+
 struct LaunchOpts {
     bool pdl = false;          // programmatic dependent launch (overlap with the previous kernel)
     void* scratch = nullptr;   // MMA-path scratch of xprep_bytes(N, K), zeroed when new (nullptr: internal)
+    const MmaFeed* feed = nullptr;  // MMA path: this launch prepares the next launch's x
+    bool x_ready = false;           // MMA path: the previous launch prepared this launch's x
 };
 
 // MMA path (gemv_mma.cu): scratch bytes for one x vector of length K, the
@@ -25,7 +40,7 @@ void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K);
 size_t static_scratch_bytes();
 cudaError_t static_scratch(void** out);
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K, void* scratch,
-                            cudaStream_t stream, bool pdl);
+                            cudaStream_t stream, bool pdl, const MmaFeed* feed = nullptr, bool x_ready = false);
 // Several MMA-layout matrices of one type that multiply the same x (same K)
 // in one launch: y_s = W_s x for s < nseg <= MMA_MAX_SEGMENTS, scratch of
 // xprep_bytes(sum of N_s, K).
@@ -48,7 +63,8 @@ struct PeerExchange {
     int64_t xo[4];                     // segment s's first float in the exchange buffer
 };
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
-                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr);
+                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr,
+                                  const MmaFeed* feed = nullptr, bool x_ready = false);
 // Copy the peers' rows of each segment from this GPU's exchange buffer into
 // the full outputs once every peer's flag reaches `epoch` (a bounded wait:
 // on time-out it sets *err and copies nothing).

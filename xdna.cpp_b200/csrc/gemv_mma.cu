@@ -95,7 +95,9 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //           register of the pair is zero, so the kernel needs no selects.
 //   zeros   32 zero bytes: the B "slot" of the 24 lanes that supply nothing
 //   scale   2^e per 32-value block;  xsum  sum of the block's x
-//   count   one arrival counter per tile (zeroed by xprep_kernel)
+//   count   one arrival counter per tile, the CTA completion counter and one
+//           per 32-value chunk of a feeding output (cleared by xprep_kernel,
+//           or by the previous launch when it prepared x)
 //   partial kMaxCtas CTAs * 2 slots * 16 floats (level-2 CTA sums)
 // ---------------------------------------------------------------------------
 // One CTA of 24 warps per SM: warps of one CTA are scheduled as equals,
@@ -117,70 +119,76 @@ __device__ __forceinline__ uint32_t digit_word(uint32_t v0, uint32_t v1, uint32_
     return __byte_perm(__byte_perm(v0, v1, sel), __byte_perm(v2, v3, sel), 0x5410);
 }
 
-// x preparation: one warp per 32-value block (lane j = value j); also zeroes
-// the tile counters of the GEMV that follows.
+// x preparation of 32 consecutive values x[32 w32 + lane] held one per lane
+// (one 32-value block, or two 16-value blocks when BL = 16): the block scale
+// 2^e, the block sum and the three digit planes, written to the fragment slots.
 // BL = values per x block (B column): 32, or 16 for the formats with
 // 16-value sub-blocks (chunks 0-3 then cover blocks 0-7, chunks 4-7 blocks
 // 8-15 of the group).
 template <int BL>
+__device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t* __restrict__ frags,
+                                         float* __restrict__ scale, float* __restrict__ xsum) {
+    const int64_t b = (w32 * 32 + lane) / BL;  // this lane's block
+    float m = fabsf(v), s = v;
+#pragma unroll
+    for (int o = BL / 2; o > 0; o >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+    }
+    int E = 0;
+    if (m > 0.f) frexpf(m, &E);  // m < 2^E
+    int e = m > 0.f ? E - 22 : 0;
+    e = e < -120 ? -120 : (e > 120 ? 120 : e);
+    const int X = __float2int_rn(v * ldexpf(1.0f, -e));  // |X| <= 2^22
+    const int d0 = ((X + 128) & 255) - 128;
+    const int X1 = (X - d0) >> 8;
+    const int d1 = ((X1 + 128) & 255) - 128;
+    const int d2 = (X1 - d1) >> 8;                        // |d2| <= 64
+    const uint32_t mine = (static_cast<uint32_t>(d0) & 0xFFu) | ((static_cast<uint32_t>(d1) & 0xFFu) << 8) |
+                          ((static_cast<uint32_t>(d2) & 0xFFu) << 16);
+    const uint32_t n1 = __shfl_down_sync(0xffffffffu, mine, 1);
+    const uint32_t n2 = __shfl_down_sync(0xffffffffu, mine, 2);
+    const uint32_t n3 = __shfl_down_sync(0xffffffffu, mine, 3);
+    if ((lane & 3) == 0) {  // values 4c' .. 4c' + 3 of the block, c' = (lane % BL) / 4
+        const uint32_t D0 = digit_word(mine, n1, n2, n3, 0);
+        const uint32_t D1 = digit_word(mine, n1, n2, n3, 1);
+        const uint32_t D2 = digit_word(mine, n1, n2, n3, 2);
+        constexpr int kPerGroup = 256 / BL;
+        const int64_t gi = b / kPerGroup;
+        const int jb = static_cast<int>(b % kPerGroup);
+        const int blk = jb & 7;                                          // B column
+        const int c = (BL == 32 ? 0 : 4 * (jb >> 3)) + (lane % BL) / 4;  // chunk
+        uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
+        if (blk < 4) {
+            slot[0] = make_uint4(D0, 0u, D1, 0u);
+            slot[1] = make_uint4(D2, 0u, 0u, 0u);
+        } else {
+            slot[0] = make_uint4(0u, D0, 0u, D1);
+            slot[1] = make_uint4(0u, D2, 0u, 0u);
+        }
+    }
+    if (lane % BL == 0) {
+        scale[b] = ldexpf(1.0f, e);
+        xsum[b] = s;
+    }
+}
+
+// x preparation: one warp per 32 values (lane j = value j); also clears the
+// counters (ncount ints) of the GEMV that follows.
+template <int BL>
 __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, int64_t K, uint8_t* __restrict__ frags,
                                                     uint8_t* __restrict__ zeros, float* __restrict__ scale,
                                                     float* __restrict__ xsum, int* __restrict__ count,
-                                                    int64_t ntiles) {
+                                                    int64_t ncount) {
     pdl_release();
     pdl_wait();
     const int64_t gtid = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
     const int64_t nthr = int64_t(gridDim.x) * blockDim.x;
-    for (int64_t i = gtid; i < ntiles; i += nthr) count[i] = 0;
+    for (int64_t i = gtid; i < ncount; i += nthr) count[i] = 0;
     if (gtid < kSlotBytes / 4) reinterpret_cast<uint32_t*>(zeros)[gtid] = 0u;
     const int lane = threadIdx.x & 31;
-    const int64_t nw = K / 32;  // one warp per 32 values (32 / BL blocks)
-    for (int64_t w32 = gtid >> 5; w32 < nw; w32 += nthr >> 5) {
-        const int64_t b = (w32 * 32 + lane) / BL;  // this lane's block
-        const float v = x[w32 * 32 + lane];
-        float m = fabsf(v), s = v;
-#pragma unroll
-        for (int o = BL / 2; o > 0; o >>= 1) {
-            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            s += __shfl_xor_sync(0xffffffffu, s, o);
-        }
-        int E = 0;
-        if (m > 0.f) frexpf(m, &E);  // m < 2^E
-        int e = m > 0.f ? E - 22 : 0;
-        e = e < -120 ? -120 : (e > 120 ? 120 : e);
-        const int X = __float2int_rn(v * ldexpf(1.0f, -e));  // |X| <= 2^22
-        const int d0 = ((X + 128) & 255) - 128;
-        const int X1 = (X - d0) >> 8;
-        const int d1 = ((X1 + 128) & 255) - 128;
-        const int d2 = (X1 - d1) >> 8;                        // |d2| <= 64
-        const uint32_t mine = (static_cast<uint32_t>(d0) & 0xFFu) | ((static_cast<uint32_t>(d1) & 0xFFu) << 8) |
-                              ((static_cast<uint32_t>(d2) & 0xFFu) << 16);
-        const uint32_t n1 = __shfl_down_sync(0xffffffffu, mine, 1);
-        const uint32_t n2 = __shfl_down_sync(0xffffffffu, mine, 2);
-        const uint32_t n3 = __shfl_down_sync(0xffffffffu, mine, 3);
-        if ((lane & 3) == 0) {  // values 4c' .. 4c' + 3 of the block, c' = (lane % BL) / 4
-            const uint32_t D0 = digit_word(mine, n1, n2, n3, 0);
-            const uint32_t D1 = digit_word(mine, n1, n2, n3, 1);
-            const uint32_t D2 = digit_word(mine, n1, n2, n3, 2);
-            constexpr int kPerGroup = 256 / BL;
-            const int64_t gi = b / kPerGroup;
-            const int jb = static_cast<int>(b % kPerGroup);
-            const int blk = jb & 7;                                       // B column
-            const int c = (BL == 32 ? 0 : 4 * (jb >> 3)) + (lane % BL) / 4;  // chunk
-            uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
-            if (blk < 4) {
-                slot[0] = make_uint4(D0, 0u, D1, 0u);
-                slot[1] = make_uint4(D2, 0u, 0u, 0u);
-            } else {
-                slot[0] = make_uint4(0u, D0, 0u, D1);
-                slot[1] = make_uint4(0u, D2, 0u, 0u);
-            }
-        }
-        if (lane % BL == 0) {
-            scale[b] = ldexpf(1.0f, e);
-            xsum[b] = s;
-        }
-    }
+    const int64_t nw = K / 32;
+    for (int64_t w32 = gtid >> 5; w32 < nw; w32 += nthr >> 5) prep_x32<BL>(x[w32 * 32 + lane], w32, lane, frags, scale, xsum);
 }
 
 // One launch covers up to kMaxSegs weight matrices that share x (and K):
@@ -204,6 +212,19 @@ struct GemvArgs {
     bool xchg;      // row-sharded launch: also store rows into the peers' exchange buffers
     PeerExchange x;
     int* done;      // CTAs finished (zeroed by xprep_kernel), for the completion flags
+    // feed: tiles [f_t0, f_t1) (output f_y) are the next launch's x; its
+    // fragments, scales and sums go to f_frags / f_scale / f_xsum; f_chunk
+    // counts the two tiles of each 32-value chunk in (f_bl = 0: no feed)
+    uint8_t* f_frags;
+    float* f_scale;
+    float* f_xsum;
+    int* f_chunk;
+    const float* f_y;
+    int64_t f_t0, f_t1;
+    int f_bl;
+    int* f_count;       // the next launch's counters (f_ncount ints) and zero slot, cleared here
+    int64_t f_ncount;
+    uint32_t* f_zeros;
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -573,6 +594,28 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         group_dot_nib<TYPE>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
 
+// After a warp has written all 16 rows of `tile`: if the tile feeds the next
+// launch, count it in at its 32-value chunk; the second of the chunk's two
+// tiles (in any CTA) prepares the chunk as the x-preparation kernel would.
+// Called once per emitted tile and kept out of line, so that it adds nothing
+// to the register budget of the streaming loop.
+__device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum, int* chunk, const float* y, int lt,
+                                      int bl, int lane) {
+    const int ch = lt >> 1;  // lt: the tile's index within the feeding output
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0) prev = atomicAdd(chunk + ch, 1);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev == 0) return;
+    __threadfence();
+    const float v = __ldcg(y + int64_t(ch) * 32 + lane);
+    if (bl == 16)
+        prep_x32<16>(v, ch, lane, frags, scale, xsum);
+    else
+        prep_x32<32>(v, ch, lane, frags, scale, xsum);
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(const GemvArgs a) {
     // unit, tile and group counts fit in 32 bits (the launcher checks)
@@ -593,7 +636,14 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         for (int d = 0; d < kPrefetch && u0 + d < u1; ++d)
             prefetch_l2(unit_weights<TYPE>(a, u0 + d), kUnitBytes<TYPE>);
     pdl_release();
-    pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel
+    pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel (or the previous launch)
+    if (a.f_bl != 0) {
+        // what the x-preparation kernel would clear for the next launch; its
+        // scratch slot's previous user has completed (this launch waited on it)
+        const int64_t gt = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+        for (int64_t i = gt; i < a.f_ncount; i += int64_t(gridDim.x) * blockDim.x) a.f_count[i] = 0;
+        if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
+    }
 
     const bool supplier = g == t || g == t + 4;
     const uint8_t* fb0 = supplier ? a.frags + g * kSlotBytes : a.zeros;
@@ -626,11 +676,13 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             const SegRef sr = seg_ref(a, tile);
             ty = sr.y + (tile - static_cast<int>(sr.first_tile)) * MMA_TILE_ROWS;
         }
+        bool emitted = false;  // this warp wrote the tile's 16 rows (warp-uniform)
         if (u == tbeg && gend == ng) {  // the whole tile is this warp's
             if (t == 0) {
                 emit(a, ty, tile, g, y0);
                 emit(a, ty, tile, g + 8, y8);
             }
+            emitted = true;
         } else {
             // the tile's contributors are global warps wa..wb; this CTA holds lo..hi of them
             const int wa = static_cast<int>(warp_of(tbeg, U, NW)), wb = static_cast<int>(warp_of(tbeg + ng - 1, U, NW));
@@ -658,6 +710,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                 const int ca = wa / kWarps, cb = wb / kWarps;
                 if (ca == cb) {  // every contributor was in this CTA
                     if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc);
+                    emitted = true;
                 } else {
                     // level 2: the CTA's sum to global memory; the last CTA adds them in CTA order.
                     // A CTA shares at most two tiles with others: its first (slot 0) and last (slot 1).
@@ -686,10 +739,13 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                         }
                         sum += __shfl_xor_sync(0xffffffffu, sum, 16);
                         if (h == 0) emit(a, ty, tile, r, sum);
+                        emitted = true;
                     }
                 }
             }
         }
+        if (emitted && a.f_bl != 0 && tile >= a.f_t0 && tile < a.f_t1)
+            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl, lane);
         u = tbeg + gend;
     }
     if (a.xchg) {
@@ -869,6 +925,12 @@ int g_scratch_n = 0;
 
 }  // namespace
 
+// Counters of a launch over `ntiles` tiles: one per tile, the CTA completion
+// counter, and one per 32-value chunk of an output that feeds the next launch.
+// All start at zero: cleared by the x-preparation kernel, or by the launch
+// before when that one prepares x.
+static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1; }
+
 // Scratch of one MMA GEMV launch (layout described above the kernels).
 ScratchLayout scratch_layout(int64_t N, int64_t K) {
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
@@ -880,7 +942,7 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
     L.scale = up(L.zeros + kSlotBytes);
     L.xsum = up(L.scale + 2 * nblk * sizeof(float));  // room for 16-value blocks
     L.count = up(L.xsum + 2 * nblk * sizeof(float));
-    L.partial = up(L.count + (ntiles + 1) * sizeof(int));  // + the CTA completion counter
+    L.partial = up(L.count + counter_ints(static_cast<int64_t>(ntiles)) * sizeof(int));
     L.total = up(L.partial + size_t(kMaxCtas) * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
 }
@@ -930,13 +992,14 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
 }
 
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
-                            void* scratch, cudaStream_t stream, bool pdl) {
+                            void* scratch, cudaStream_t stream, bool pdl, const MmaFeed* feed, bool x_ready) {
     const MmaSegment seg{W, y, N};
-    return gemv_mma_multi_launch(type, &seg, 1, x, K, scratch, stream, pdl);
+    return gemv_mma_multi_launch(type, &seg, 1, x, K, scratch, stream, pdl, nullptr, feed, x_ready);
 }
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
-                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg) {
+                                  void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg,
+                                  const MmaFeed* feed, bool x_ready) {
     if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K &&
          type != T_IQ4_XS) ||
         nseg < 1 || nseg > kMaxSegs)
@@ -969,6 +1032,27 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     a.partial = reinterpret_cast<float*>(base + L.partial);
     a.ngroups = ngroups;
     a.units = ntiles * ngroups;
+    if (feed) {
+        // the next launch's x is segment feed->seg in full: K_next = its N
+        if (xchg || !feed->next_scratch || feed->seg < 0 || feed->seg >= nseg || segs[feed->seg].N % 256 != 0 ||
+            (feed->bl != 16 && feed->bl != 32) || feed->next_rows <= 0 || feed->next_rows % MMA_TILE_ROWS != 0)
+            return cudaErrorInvalidValue;
+        const ScratchLayout Ln = scratch_layout(MMA_TILE_ROWS, segs[feed->seg].N);  // x offsets depend on K only
+        uint8_t* nb = static_cast<uint8_t*>(feed->next_scratch);
+        a.f_frags = nb + Ln.frags;
+        a.f_scale = reinterpret_cast<float*>(nb + Ln.scale);
+        a.f_xsum = reinterpret_cast<float*>(nb + Ln.xsum);
+        a.f_chunk = a.count + ntiles + 1;
+        a.f_y = segs[feed->seg].y;
+        a.f_t0 = feed->seg > 0 ? a.tile_end[feed->seg - 1] : 0;
+        a.f_t1 = a.tile_end[feed->seg];
+        a.f_bl = feed->bl;
+        const int64_t nt = feed->next_rows / MMA_TILE_ROWS;
+        const ScratchLayout Lf = scratch_layout(feed->next_rows, segs[feed->seg].N);
+        a.f_count = reinterpret_cast<int*>(nb + Lf.count);
+        a.f_ncount = counter_ints(nt);
+        a.f_zeros = reinterpret_cast<uint32_t*>(nb + Lf.zeros);
+    }
     if (a.units >= (int64_t(1) << 31)) return cudaErrorInvalidValue;  // the kernel counts units in 32 bits
 
     static int s_sms[16] = {};
@@ -1001,14 +1085,16 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cp.stream = stream;
     cp.attrs = attr;
     cp.numAttrs = 1;
-    cudaError_t e = mma_blk16(type)
-                        ? cudaLaunchKernelEx(&cp, xprep_kernel<16>, x, K, base + L.frags, base + L.zeros,
-                                             reinterpret_cast<float*>(base + L.scale),
-                                             reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1)
-                        : cudaLaunchKernelEx(&cp, xprep_kernel<32>, x, K, base + L.frags, base + L.zeros,
-                                             reinterpret_cast<float*>(base + L.scale),
-                                             reinterpret_cast<float*>(base + L.xsum), a.count, ntiles + 1);
-    if (e != cudaSuccess) return e;
+    if (!x_ready) {  // else the previous launch's epilogue prepared x (and the counters are clear)
+        cudaError_t e = mma_blk16(type)
+                            ? cudaLaunchKernelEx(&cp, xprep_kernel<16>, x, K, base + L.frags, base + L.zeros,
+                                                 reinterpret_cast<float*>(base + L.scale),
+                                                 reinterpret_cast<float*>(base + L.xsum), a.count, counter_ints(ntiles))
+                            : cudaLaunchKernelEx(&cp, xprep_kernel<32>, x, K, base + L.frags, base + L.zeros,
+                                                 reinterpret_cast<float*>(base + L.scale),
+                                                 reinterpret_cast<float*>(base + L.xsum), a.count, counter_ints(ntiles));
+        if (e != cudaSuccess) return e;
+    }
 
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks));
