@@ -122,7 +122,7 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -443,8 +443,16 @@ def run_b200_arm(args, dist: Dist) -> None:
     e2e_ms = dist.max((time.perf_counter() - t0) * 1000.0 / args.steps)
     dist.barrier()
 
-    # dominant kernel alone (local shards, no collectives)
-    k_ms = dist.max(kernel_only_ms(torch, G, model, max(2, args.steps // 2)))
+    # the dominant kernel's device time per step.  On one GPU the timed step is
+    # the GEMV chain alone (each launch prepares the next one's x; one x
+    # preparation kernel per step), so its own CUDA-event time is used.  With
+    # N GPUs the step also holds the row exchange: the GEMV launches are timed
+    # alone instead (b200_gemv / b200_gemv_multi, an x preparation per launch).
+    if dist.world == 1:
+        k_ms, k_src = ms_step, "the timed compute_graph step (CUDA events on the backend stream)"
+    else:
+        k_ms = dist.max(kernel_only_ms(torch, G, model, max(2, args.steps // 2)))
+        k_src = "GEMV launches alone per step (b200_gemv / b200_gemv_multi replayed as a CUDA graph)"
     peak, peak_src = measured_peak()
     traffic, traffic_src = profiled_traffic() if dist.world == 1 else (None, "profiled at N=1 only")
     achieved = model.local_bytes / (k_ms * 1e-3) / 1e9
@@ -475,16 +483,19 @@ def run_b200_arm(args, dist: Dist) -> None:
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "tok_s": round(1000.0 / e2e_ms, 3),
                     "h2d_bytes_per_step": 3 * HIDDEN * 4, "d2h_bytes_per_step": VOCAB * 4,
                     "path": "ggml_backend_xdna_compute_graph, token input from pinned host memory, logits to host"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<12> (Q4_K) with its xprep_kernel",
+            "roofline": {"bound": "hbm", "kernel": "gemv_mma_kernel<12> (Q4_K)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)",
                          "traffic": traffic, "traffic_unit": "bytes per step (all GEMV launches)",
-                         "traffic_source": traffic_src, "algorithmic_bytes_per_step": model.local_bytes, "per_launch_note": f"{LAUNCHES_PER_TOKEN} GEMV launches per step (q/k/v and gate/up "
-                         "fused); achieved = local weight bytes per step / GEMV-only device time per step"},
+                         "traffic_source": traffic_src, "algorithmic_bytes_per_step": model.local_bytes,
+                         "per_launch_note": f"{LAUNCHES_PER_TOKEN} GEMV launches per step (q/k/v and gate/up "
+                         "fused); achieved = local weight bytes per step / device time per step of " + k_src},
             "clocks": clk.summary(),
-            # per launch group (q/k/v and gate/up fused, o, down, lm_head):
-            # xprep_kernel + gemv_mma_kernel; NCCL's all-gather kernels not counted
-            "gpu_launches": args.steps * LAUNCHES_PER_TOKEN * 2,
+            # one GPU: 321 gemv_mma_kernel launches + one xprep_kernel per step
+            # (every later launch's x is prepared by the launch before it);
+            # N GPUs: xprep_kernel + gemv_mma_kernel + xchg_gather_kernel per
+            # launch group (NCCL's kernels, on the fallback path, not counted)
+            "gpu_launches": args.steps * (LAUNCHES_PER_TOKEN + 1 if dist.world == 1 else LAUNCHES_PER_TOKEN * 3),
         }
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -496,7 +507,7 @@ def run_b200_arm(args, dist: Dist) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
