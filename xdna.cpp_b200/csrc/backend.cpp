@@ -318,7 +318,7 @@ struct Backend {
         char* local = nullptr;
         char* peer[kMaxPeers] = {};
         size_t cap_floats = 0;  // floats per data half
-        uint32_t epoch = 0;
+        uint32_t* epoch = nullptr;  // the device epoch counter (a word of the local flag region)
         int* err = nullptr;     // set by a gather kernel whose wait timed out
     } xg;
     // CUDA graph of the last node list seen twice in a row with every operand
@@ -363,8 +363,10 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
 
 bool nccl_wait(ncclComm_t comm, ncclResult_t r, const char* what);
 
-// Exchange regions: [flags: one uint32 per source rank, 256 B][half 0][half 1].
+// Exchange regions: [flags: one uint32 per source rank, then this rank's
+// epoch counter at byte 128; 256 B][half 0][half 1].
 constexpr size_t kXchgFlagBytes = 256;
+constexpr size_t kXchgEpochOffset = 128;
 
 void release_exchange(Backend* be) {
     Backend::Exchange& x = be->xg;
@@ -430,6 +432,7 @@ bool setup_exchange(Backend* be) {
         release_exchange(be);
         return false;
     }
+    x.epoch = reinterpret_cast<uint32_t*>(x.local + kXchgEpochOffset);  // zero: cleared with the region
     x.ok = true;
     return true;
 }
@@ -1013,10 +1016,10 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n, const MmaPlan* plan 
         PeerExchange pe = {};
         pe.world = be->world;
         pe.rank = be->rank;
-        pe.epoch = ++xg.epoch;
-        const size_t half = kXchgFlagBytes + (pe.epoch & 1u) * xg.cap_floats * sizeof(float);
+        pe.half_floats = static_cast<int64_t>(xg.cap_floats);
+        pe.epoch = xg.epoch;
         for (int p = 0; p < be->world; ++p) {
-            pe.peer_data[p] = reinterpret_cast<float*>(xg.peer[p] + half);
+            pe.peer_data[p] = reinterpret_cast<float*>(xg.peer[p] + kXchgFlagBytes);
             pe.peer_flags[p] = reinterpret_cast<uint32_t*>(xg.peer[p]);
         }
         GatherSeg gs[MMA_MAX_SEGMENTS];
@@ -1026,12 +1029,14 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n, const MmaPlan* plan 
             gs[k] = GatherSeg{f[k].y_full, f[k].seg.N, off};
             off += f[k].n_out;
         }
+        // a planned feed is done by the gather, which holds the full output
         return cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream,
-                                             true, &pe),
+                                             true, &pe, nullptr, plan && plan->x_ready),
                        "sharded gemv launch") &&
-               cuda_ok(xchg_gather_launch(reinterpret_cast<const float*>(xg.local + half),
-                                          reinterpret_cast<const uint32_t*>(xg.local), pe.epoch, be->world, be->rank,
-                                          gs, static_cast<int>(n), xg.err, be->stream),
+               cuda_ok(xchg_gather_launch(reinterpret_cast<const float*>(xg.local + kXchgFlagBytes),
+                                          static_cast<int64_t>(xg.cap_floats),
+                                          reinterpret_cast<const uint32_t*>(xg.local), xg.epoch, be->world, be->rank,
+                                          gs, static_cast<int>(n), xg.err, be->stream, plan ? plan->feed : nullptr),
                        "exchange gather launch");
     }
     if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream, true,
@@ -1271,13 +1276,20 @@ static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
         r.nf = no_fuse ? (fusable(be, node, &r.f[0]) ? 1 : 0) : fused_run_length(be, nodes, i, n_nodes, r.f);
         r.count = !no_fuse && r.nf > 1 ? r.nf : 1;
         r.fused = !no_fuse && (r.nf > 1 || (r.nf == 1 && r.f[0].sharded && be->xg.ok));
+        // planned: a device-resident MMA launch that is either local or
+        // sharded over the peer exchange (whose gather holds the full output)
         r.planned = r.nf > 0;
         const size_t nseg = r.fused ? r.nf : 1;
-        int64_t rows = 0;
+        int64_t rows = 0, full = 0;
+        size_t nsharded = 0;
         for (size_t j = 0; j < nseg && r.planned; ++j) {
-            r.planned = !r.f[j].sharded;
+            nsharded += r.f[j].sharded ? 1 : 0;
             rows += r.f[j].seg.N;
+            full += r.f[j].n_out;
         }
+        if (nsharded > 0)
+            r.planned = r.planned && r.fused && nsharded == nseg && be->xg.ok &&
+                        static_cast<size_t>(full) <= be->xg.cap_floats;
         r.rows = rows;
         if (r.planned) need = std::max(need, xprep_bytes(rows, r.f[0].K));
         runs.push_back(r);
@@ -1294,7 +1306,7 @@ static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
         if (!r.planned || !q.planned || r.plan.scratch == q.plan.scratch) continue;
         const size_t nseg = r.fused ? r.nf : 1;
         for (size_t j = 0; j < nseg; ++j)
-            if (r.f[j].seg.y == q.f[0].x && r.f[j].seg.N == q.f[0].K) {
+            if (r.f[j].y_full == q.f[0].x && r.f[j].n_out == q.f[0].K) {
                 r.feed.next_scratch = q.plan.scratch;
                 r.feed.next_rows = q.rows;
                 r.feed.seg = static_cast<int>(j);
@@ -1330,7 +1342,7 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
     std::lock_guard<std::mutex> lk(be->mtx);
     DeviceGuard g(be->dev);
     static const bool no_graph = getenv("XDNA_B200_NO_GRAPH") != nullptr || getenv("XDNA_TRACE_NODES") != nullptr;
-    if (!no_graph && be->world == 1) {
+    if (!no_graph) {
         std::vector<uint64_t> sig;
         graph_signature(nodes, n_nodes, &sig);
         if (sig == be->graph_sig && be->graph_ok_sig) {

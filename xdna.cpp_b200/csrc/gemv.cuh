@@ -54,27 +54,35 @@ struct MmaSegment {
 // mapped over NVLink) and, when all its CTAs are done, raises its flag
 // (= epoch) in every peer's flag array.  A gather kernel on each GPU then
 // waits for the peers' flags and copies their rows into the full outputs.
+// The epoch lives on the device (no launch argument changes from one launch
+// to the next, so a step can be replayed as a CUDA graph): launch e reads
+// e - 1 from *epoch, uses data half e % 2, and its last CTA stores e.
 constexpr int kMaxPeers = 8;
 struct PeerExchange {
-    float* peer_data[kMaxPeers];       // each rank's exchange buffer for this launch
+    float* peer_data[kMaxPeers];       // each rank's exchange buffer, half 0 (half 1 follows)
     uint32_t* peer_flags[kMaxPeers];   // each rank's flag array (one word per source rank)
     int world, rank;
-    uint32_t epoch;
+    int64_t half_floats;               // floats per data half
+    uint32_t* epoch;                   // this rank's epoch counter (device memory)
     int64_t xo[4];                     // segment s's first float in the exchange buffer
 };
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr,
                                   const MmaFeed* feed = nullptr, bool x_ready = false);
-// Copy the peers' rows of each segment from this GPU's exchange buffer into
-// the full outputs once every peer's flag reaches `epoch` (a bounded wait:
-// on time-out it sets *err and copies nothing).
+// Copy the peers' rows of each segment from this GPU's exchange buffer
+// (xdata: half 0) into the full outputs once every peer's flag reaches the
+// launch's epoch, read from *epoch after the GEMV has stored it (a bounded
+// wait: on time-out it sets *err and copies nothing).  With a feed (seg =
+// index into segs) the gather also prepares that full output as the next
+// launch's x, as a feeding GEMV would.
 struct GatherSeg {
     float* y_full;
     int64_t n_local;
     int64_t xo;
 };
-cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32_t epoch, int world, int rank,
-                               const GatherSeg* segs, int nseg, int* err, cudaStream_t stream);
+cudaError_t xchg_gather_launch(const float* xdata, int64_t half_floats, const uint32_t* flags,
+                               const uint32_t* epoch, int world, int rank, const GatherSeg* segs, int nseg, int* err,
+                               cudaStream_t stream, const MmaFeed* feed = nullptr);
 cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N, int64_t K, bool pack,
                               cudaStream_t stream);
 

@@ -246,12 +246,13 @@ __device__ __forceinline__ SegRef seg_ref(const GemvArgs& a, int64_t tile) {
 
 // Output row `row` (0..15) of global tile `tile`: to y, and for a sharded
 // launch to the same place of every peer's exchange buffer (NVLink stores).
-__device__ __forceinline__ void emit(const GemvArgs& a, float* ty, int tile, int row, float v) {
+// hoff: the launch's exchange data half (sharded launches)
+__device__ __forceinline__ void emit(const GemvArgs& a, float* ty, int tile, int row, float v, int64_t hoff) {
     ty[row] = v;
     if (a.xchg) {
         const SegRef sr = seg_ref(a, tile);
         const int64_t n_local = (sr.end_tile - sr.first_tile) * MMA_TILE_ROWS;
-        const int64_t off = sr.xo + a.x.rank * n_local + (tile - sr.first_tile) * MMA_TILE_ROWS + row;
+        const int64_t off = hoff + sr.xo + a.x.rank * n_local + (tile - sr.first_tile) * MMA_TILE_ROWS + row;
 #pragma unroll
         for (int p = 0; p < kMaxPeers; ++p)
             if (p < a.x.world && p != a.x.rank) a.x.peer_data[p][off] = v;
@@ -637,6 +638,12 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             prefetch_l2(unit_weights<TYPE>(a, u0 + d), kUnitBytes<TYPE>);
     pdl_release();
     pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel (or the previous launch)
+    uint32_t xe = 0;  // sharded: this launch's epoch and exchange data half
+    int64_t hoff = 0;
+    if (a.xchg) {
+        xe = __ldcg(a.x.epoch) + 1u;
+        hoff = (xe & 1u) ? a.x.half_floats : 0;
+    }
     if (a.f_bl != 0) {
         // what the x-preparation kernel would clear for the next launch; its
         // scratch slot's previous user has completed (this launch waited on it)
@@ -679,8 +686,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         bool emitted = false;  // this warp wrote the tile's 16 rows (warp-uniform)
         if (u == tbeg && gend == ng) {  // the whole tile is this warp's
             if (t == 0) {
-                emit(a, ty, tile, g, y0);
-                emit(a, ty, tile, g + 8, y8);
+                emit(a, ty, tile, g, y0, hoff);
+                emit(a, ty, tile, g + 8, y8, hoff);
             }
             emitted = true;
         } else {
@@ -709,7 +716,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     acc += s_part[((v - cta * kWarps) * 2 + (v == wa ? slot_a : 0)) * MMA_TILE_ROWS + r];
                 const int ca = wa / kWarps, cb = wb / kWarps;
                 if (ca == cb) {  // every contributor was in this CTA
-                    if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc);
+                    if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc, hoff);
                     emitted = true;
                 } else {
                     // level 2: the CTA's sum to global memory; the last CTA adds them in CTA order.
@@ -738,7 +745,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                             for (int j = 0; j < 8; ++j) sum += part[j];
                         }
                         sum += __shfl_xor_sync(0xffffffffu, sum, 16);
-                        if (h == 0) emit(a, ty, tile, r, sum);
+                        if (h == 0) emit(a, ty, tile, r, sum, hoff);
                         emitted = true;
                     }
                 }
@@ -761,7 +768,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
                 __threadfence_system();
                 for (int p = 0; p < a.x.world; ++p)
-                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, a.x.epoch);
+                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, xe);
+                *a.x.epoch = xe;  // every CTA has read e - 1 (before counting in)
             }
         }
     }
@@ -783,16 +791,30 @@ struct GatherArgs {
     GatherSeg seg[kMaxSegs];
     int nseg;
 };
-__global__ void __launch_bounds__(256) xchg_gather_kernel(const float* __restrict__ xdata, const uint32_t* flags,
-                                                          uint32_t epoch, int world, int rank, const GatherArgs g,
-                                                          int* err) {
+// Feed of a gather: the next launch's x is gathered segment f.seg in full.
+struct GatherFeed {
+    int seg, bl;  // bl = 0: no feed
+    uint8_t* frags;
+    float* scale;
+    float* xsum;
+    int* count;  // the next launch's counters (ncount ints) and zero slot, cleared here
+    int64_t ncount;
+    uint32_t* zeros;
+};
+__global__ void __launch_bounds__(256) xchg_gather_kernel(const float* __restrict__ xdata, int64_t half_floats,
+                                                          const uint32_t* flags, const uint32_t* epoch, int world,
+                                                          int rank, const GatherArgs g, int* err, const GatherFeed f) {
     __shared__ int s_ok;
+    // The GEMV has finished and stored this launch's epoch; the gather does
+    // not let the next kernel start early, so the counter stays e until then.
+    pdl_wait();
+    const uint32_t e = __ldcg(epoch);
     if (threadIdx.x == 0) {
         int ok = 1;
         const uint64_t t0 = global_ns();
         for (int p = 0; p < world && ok; ++p) {
             if (p == rank) continue;
-            while (static_cast<int32_t>(ld_acquire_sys(flags + p) - epoch) < 0) {
+            while (static_cast<int32_t>(ld_acquire_sys(flags + p) - e) < 0) {
                 if (global_ns() - t0 > kGatherWaitNs) {
                     ok = 0;
                     atomicExch(err, 1);
@@ -804,17 +826,43 @@ __global__ void __launch_bounds__(256) xchg_gather_kernel(const float* __restric
         s_ok = ok;
     }
     __syncthreads();
-    pdl_wait();  // this GPU's GEMV has finished (its own rows are in y)
     if (!s_ok) return;
+    const float* xd = xdata + ((e & 1u) ? half_floats : 0);
+    const int64_t gt = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+    if (f.bl != 0) {
+        for (int64_t i = gt; i < f.ncount; i += stride) f.count[i] = 0;
+        if (gt < kSlotBytes / 4) f.zeros[gt] = 0u;
+    }
     for (int s = 0; s < g.nseg; ++s) {
         const GatherSeg sg = g.seg[s];
+        if (f.bl != 0 && s == f.seg) {
+            // one warp per 32 values of the full output: the peers' rows are
+            // copied in, and the 32 values become the next launch's x digits
+            const int lane = threadIdx.x & 31;
+            const int64_t nch = sg.n_local * world / 32;
+            for (int64_t ch = gt >> 5; ch < nch; ch += stride >> 5) {
+                const int64_t r = ch * 32 + lane;
+                const int p = static_cast<int>(r / sg.n_local);
+                float v;
+                if (p == rank) {
+                    v = __ldcg(sg.y_full + r);
+                } else {
+                    v = __ldcg(xd + sg.xo + r);
+                    sg.y_full[r] = v;
+                }
+                if (f.bl == 16)
+                    prep_x32<16>(v, ch, lane, f.frags, f.scale, f.xsum);
+                else
+                    prep_x32<32>(v, ch, lane, f.frags, f.scale, f.xsum);
+            }
+            continue;
+        }
         for (int p = 0; p < world; ++p) {
             if (p == rank) continue;  // own rows: written by the GEMV
             float* dst = sg.y_full + p * sg.n_local;
-            const float* src = xdata + sg.xo + p * sg.n_local;
-            for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < sg.n_local; i += stride)
-                dst[i] = __ldcg(src + i);
+            const float* src = xd + sg.xo + p * sg.n_local;
+            for (int64_t i = gt; i < sg.n_local; i += stride) dst[i] = __ldcg(src + i);
         }
     }
 }
@@ -1114,8 +1162,9 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0>, a);
 }
 
-cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32_t epoch, int world, int rank,
-                               const GatherSeg* segs, int nseg, int* err, cudaStream_t stream) {
+cudaError_t xchg_gather_launch(const float* xdata, int64_t half_floats, const uint32_t* flags,
+                               const uint32_t* epoch, int world, int rank, const GatherSeg* segs, int nseg, int* err,
+                               cudaStream_t stream, const MmaFeed* feed) {
     if (nseg < 1 || nseg > kMaxSegs || world < 2 || world > kMaxPeers) return cudaErrorInvalidValue;
     GatherArgs g = {};
     int64_t total = 0;
@@ -1124,8 +1173,29 @@ cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32
         total += segs[s].n_local * world;
     }
     g.nseg = nseg;
+    GatherFeed f = {};
+    if (feed) {
+        const int64_t kn = feed->seg >= 0 && feed->seg < nseg ? segs[feed->seg].n_local * world : 0;
+        if (!feed->next_scratch || kn <= 0 || kn % 256 != 0 || (feed->bl != 16 && feed->bl != 32) ||
+            feed->next_rows <= 0 || feed->next_rows % MMA_TILE_ROWS != 0)
+            return cudaErrorInvalidValue;
+        uint8_t* nb = static_cast<uint8_t*>(feed->next_scratch);
+        const ScratchLayout Ln = scratch_layout(feed->next_rows, kn);
+        f.seg = feed->seg;
+        f.bl = feed->bl;
+        f.frags = nb + Ln.frags;
+        f.scale = reinterpret_cast<float*>(nb + Ln.scale);
+        f.xsum = reinterpret_cast<float*>(nb + Ln.xsum);
+        f.count = reinterpret_cast<int*>(nb + Ln.count);
+        f.ncount = counter_ints(feed->next_rows / MMA_TILE_ROWS);
+        f.zeros = reinterpret_cast<uint32_t*>(nb + Ln.zeros);
+    }
     int64_t blocks = (total + 2047) / 2048;  // few CTAs poll the flags; each copies 8 floats per thread
     if (blocks > 32) blocks = 32;
+    if (f.bl != 0) {  // and one warp per 32 values of the next launch's x, as the x-preparation kernel
+        const int64_t prep = (segs[f.seg].n_local * world / 32 + 7) / 8;
+        if (prep > blocks) blocks = prep < 1024 ? prep : 1024;
+    }
     if (blocks < 1) blocks = 1;
     cudaLaunchConfig_t c = {};
     c.gridDim = dim3(static_cast<unsigned>(blocks));
@@ -1136,7 +1206,7 @@ cudaError_t xchg_gather_launch(const float* xdata, const uint32_t* flags, uint32
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     c.attrs = attr;
     c.numAttrs = 1;
-    return cudaLaunchKernelEx(&c, xchg_gather_kernel, xdata, flags, epoch, world, rank, g, err);
+    return cudaLaunchKernelEx(&c, xchg_gather_kernel, xdata, half_floats, flags, epoch, world, rank, g, err, f);
 }
 
 // Fixed scratch of b200_gemv_noalloc: one static device array per device
