@@ -9,8 +9,10 @@ bytes, chained through device activations (q/k/v read h, o reads q, gate/up
 read o, down reads gate and writes h, lm_head reads h).  Non-MUL_MAT ops
 (norms, RoPE, attention, SwiGLU) stay with the host framework in this plugin
 model and are not part of the step.  With N GPUs every weight is row-sharded
-(rank r owns rows [r N/W, (r+1) N/W)) and each node is completed with an NCCL
-all-gather of the F32 slices inside ggml_backend_xdna_compute_graph.
+(rank r owns rows [r N/W, (r+1) N/W)) and each launch is completed inside
+ggml_backend_xdna_compute_graph: the GEMV stores its rows into the peers'
+exchange buffers over NVLink and a gather kernel assembles the full outputs
+(an NCCL all-gather of the F32 slices where the exchange is unavailable).
 
   value : aggregate weight GB/s of the step with activations resident in HBM
           (CUDA events on the backend stream, max over ranks)
@@ -472,7 +474,8 @@ def run_b200_arm(args, dist: Dist) -> None:
             "data": "synthetic: random-init N(0,0.02) weights quantised on the GPU to Q4_K, N(0,1) activations",
             "config": {
                 "workload": "llama3-70b-shaped Q4_K decode: 561 M=1 MUL_MATs per token "
-                            "(80 layers x q,k,v,o,gate,up,down + lm_head), rows sharded over N GPUs + NCCL all-gather",
+                            "(80 layers x q,k,v,o,gate,up,down + lm_head), rows sharded over N GPUs, outputs exchanged "
+                            "over NVLink by the GEMV and a gather kernel (NCCL all-gather fallback)",
                 "weight_bytes_per_token": WEIGHT_BYTES_PER_TOKEN, "matmuls_per_token": MATMULS_PER_TOKEN,
                 "batch": 1, "parallelism": f"rows{dist.world}",
                 "tok_s": round(1000.0 / ms_step, 3),
@@ -493,9 +496,9 @@ def run_b200_arm(args, dist: Dist) -> None:
             "clocks": clk.summary(),
             # one GPU: 321 gemv_mma_kernel launches + one xprep_kernel per step
             # (every later launch's x is prepared by the launch before it);
-            # N GPUs: xprep_kernel + gemv_mma_kernel + xchg_gather_kernel per
-            # launch group (NCCL's kernels, on the fallback path, not counted)
-            "gpu_launches": args.steps * (LAUNCHES_PER_TOKEN + 1 if dist.world == 1 else LAUNCHES_PER_TOKEN * 3),
+            # N GPUs: also one xchg_gather_kernel per launch (it prepares the
+            # next launch's x); NCCL's kernels, on the fallback path, not counted
+            "gpu_launches": args.steps * (LAUNCHES_PER_TOKEN * (1 if dist.world == 1 else 2) + 1),
         }
         if cpu is not None:
             line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
