@@ -357,10 +357,12 @@ def be_last_error() -> str:
 
 
 def kernel_only_ms(torch, G, model, steps: int) -> float:
-    """Device time of one step's GEMV launches alone (no collectives, no
-    host work): the launches compute_graph makes -- q/k/v and gate/up fused
-    (b200_gemv_multi), o, down and lm_head single (b200_gemv) -- captured once
-    as a CUDA graph and replayed, for the roofline of the dominant kernel."""
+    """Device time of one step's GEMV launches alone (no exchange, no host
+    work), for the roofline of the dominant kernel when the step itself also
+    holds the row exchange (N > 1): the launches compute_graph makes -- q/k/v
+    and gate/up fused (b200_gemv_multi), o, down and lm_head single
+    (b200_gemv), each with its x preparation -- captured once as a CUDA graph
+    and replayed."""
     import ctypes as C
 
     a = model.act

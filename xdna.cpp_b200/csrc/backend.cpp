@@ -305,8 +305,9 @@ struct Backend {
         size_t bytes;
     };
     std::vector<PendingOut> pending;
-    // x-digit scratch of the MMA GEMV path: two slots, alternated per launch so
-    // that one GEMV may overlap (PDL) the next launch's x preparation
+    // x-digit scratch of the MMA GEMV path: two slots, alternated per launch,
+    // so that a launch can write the next launch's x digits (prepared-x chain)
+    // while it reads its own
     void* xscratch[2] = {nullptr, nullptr};
     size_t xscratch_bytes = 0;
     int xscratch_next = 0;

@@ -69,14 +69,16 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 // ---------------------------------------------------------------------------
 // Work split and scratch.
 //
-// The GEMV's unit of work is one (16-row tile, 256-value group) pair, 2304
-// contiguous bytes of the MMA layout; units are numbered tile-major, so unit u
-// lives at W + u * 2304.  Each warp of the grid takes one contiguous,
-// equal-sized range of units (warp w: [w U / NW, (w + 1) U / NW)), so every
-// warp streams the same number of bytes whatever N and K are: no partial
-// waves, no idle SMs on short matrices.  A tile whose groups are split across
-// warps is combined in two levels, always adding in a fixed order
-// (deterministic results):
+// The GEMV's unit of work is one (16-row tile, 256-value group) pair, the
+// format's group bytes of the MMA layout (2304 for Q4_0 / Q4_K); units are
+// numbered tile-major, so unit u lives at W + u * group bytes.  In unit mode
+// each warp of the grid takes one contiguous, equal-sized range of units
+// (warp w: [w U / NW, (w + 1) U / NW)), so every warp streams the same number
+// of bytes whatever N and K are: no partial waves, no idle SMs on short
+// matrices.  Small launches run in tile mode instead (struct Split below):
+// whole tiles per CTA, so step 2 below never happens.  A tile whose groups are
+// split across warps is combined in two levels, always adding in a fixed
+// order (deterministic results):
 //   1. each contributor writes its 16 partial rows to shared memory (two
 //      slots per warp: a warp can share only its first and its last tile) and
 //      counts itself in with a shared-memory atomic; the CTA's last
@@ -212,7 +214,7 @@ struct GemvArgs {
     int cta_tiles;  // bound on the tiles one CTA's units touch (shared-memory counters)
     bool xchg;      // row-sharded launch: also store rows into the peers' exchange buffers
     PeerExchange x;
-    int* done;      // CTAs finished (zeroed by xprep_kernel), for the completion flags
+    int* done;      // CTAs finished (cleared with the counters), for the completion flags
     // feed: tiles [f_t0, f_t1) (output f_y) are the next launch's x; its
     // fragments, scales and sums go to f_frags / f_scale / f_xsum; f_chunk
     // counts the two tiles of each 32-value chunk in (f_bl = 0: no feed)
