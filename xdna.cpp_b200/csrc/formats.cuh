@@ -383,22 +383,36 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //                with bits 2 and 3 swapped (iq4_code), which pairs codes i and
 //                i + 8 on values of one sign for the two-table decode;
 //   [2048, 2176) the 16 rows' first 8 block bytes {d, scales_h, scales_l[4]}.
+//
+// IQ3_S (9-bit indices into the 512-entry grid, one per 4 values, a sign bit
+// per value, 4-bit scales per 32): A register k of chunk c is grid entry
+// 8 (block) + c of its row, so each register is one lookup:
+//   [0, 1024)    per lane 32 B: word c, byte k = the entry's low 8 index bits;
+//   [1024, 1536) per lane 16 B: word c / 2, bits 16 (c % 2) + 4 k .. + 3 = the
+//                register's 4 sign bits, in value order;
+//   [1536, 1664) per lane 4 B: bit 4 c + k = the entry's index bit 8;
+//   [1664, 1696) the 16 rows' fp16 d;  [1696, 1760) the 16 rows' scales[4].
 XB_HD int mma_group_bytes(int type) {
     return type == T_Q5_K ? 2816
                           : (type == T_Q6_K ? 3360
-                                            : (type == T_Q3_K ? 1760 : (type == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
+                                            : ((type == T_Q3_K || type == T_IQ3_S) ? 1760
+                                                                                    : (type == T_IQ4_XS ? 2176
+                                                                                                        : MMA_GROUP_BYTES)));
 }
 XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : (type == T_Q6_K ? 3072 : 2048); }
 // GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
 XB_HD int mma_row_group_bytes(int type) {
-    return type == T_Q5_K ? 176 : (type == T_Q6_K ? 210 : (type == T_Q3_K ? 110 : (type == T_IQ4_XS ? 136 : 144)));
+    return type == T_Q5_K ? 176
+                          : (type == T_Q6_K ? 210
+                                            : ((type == T_Q3_K || type == T_IQ3_S) ? 110
+                                                                                    : (type == T_IQ4_XS ? 136 : 144)));
 }
 // x blocks (B columns) of 16 values instead of 32
 XB_HD bool mma_blk16(int type) { return type == T_Q6_K || type == T_Q3_K; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
     return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q3_K ||
-             type == T_IQ4_XS) &&
+             type == T_IQ4_XS || type == T_IQ3_S) &&
             N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0)
                ? 1
                : 0;
@@ -489,7 +503,37 @@ XB_HD int q5_plane_bit(int c, int k, int j) { return 8 * j + ((c & 1) ? 0 : 4) +
 
 // One group (gi) of one 16-row tile: GGUF rows (tile row 0 at `raw`, stride
 // row_bytes) -> MMA layout at `out` (2304 bytes), or the inverse.
+// IQ3_S grid entry e (0..63) of a row's group gi: the low index byte, the
+// index bit 8 and the 4 sign bits of its values (block bytes: d, qs[64],
+// qh[8], signs[32], scales[4])
+XB_HD uint8_t* iq3s_qs(uint8_t* row, int64_t gi, int e) { return row + gi * 110 + 2 + e; }
+XB_HD uint8_t* iq3s_qh(uint8_t* row, int64_t gi, int e) { return row + gi * 110 + 66 + (e >> 3); }
+XB_HD uint8_t* iq3s_sg(uint8_t* row, int64_t gi, int e) { return row + gi * 110 + 74 + (e >> 1); }
+
 XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64_t gi, uint8_t* out) {
+    if (type == T_IQ3_S) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            uint32_t hw = 0;
+            uint32_t sw[4] = {0, 0, 0, 0};
+            for (int c = 0; c < 8; ++c)
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = const_cast<uint8_t*>(raw) + (g + 8 * (k & 1)) * row_bytes;
+                    const int e = 8 * (t + 4 * (k >> 1)) + c;
+                    out[lane * 32 + 4 * c + k] = *iq3s_qs(row, gi, e);
+                    hw |= static_cast<uint32_t>((*iq3s_qh(row, gi, e) >> (e & 7)) & 1u) << (4 * c + k);
+                    sw[c >> 1] |= static_cast<uint32_t>((*iq3s_sg(row, gi, e) >> (4 * (e & 1))) & 0xFu)
+                                  << (16 * (c & 1) + 4 * k);
+                }
+            for (int i = 0; i < 4; ++i) put32(out + 1024 + lane * 16 + 4 * i, sw[i]);
+            put32(out + 1536 + lane * 4, hw);
+        }
+        for (int r = 0; r < 16; ++r) {
+            copy_bytes(out + 1664 + 2 * r, raw + r * row_bytes + gi * 110, 2);
+            copy_bytes(out + 1696 + 4 * r, raw + r * row_bytes + gi * 110 + 106, 4);
+        }
+        return;
+    }
     if (type == T_IQ4_XS) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;
@@ -625,6 +669,30 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 }
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
+    if (type == T_IQ3_S) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            const uint32_t hw = get32(in + 1536 + lane * 4);
+            for (int c = 0; c < 8; ++c) {
+                const uint32_t sw = get32(in + 1024 + lane * 16 + 4 * (c >> 1));
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    const int e = 8 * (t + 4 * (k >> 1)) + c;
+                    *iq3s_qs(row, gi, e) = in[lane * 32 + 4 * c + k];
+                    uint8_t* h = iq3s_qh(row, gi, e);
+                    *h = uint8_t((*h & ~(1u << (e & 7))) | (((hw >> (4 * c + k)) & 1u) << (e & 7)));
+                    uint8_t* sg = iq3s_sg(row, gi, e);
+                    const int sh = 4 * (e & 1);
+                    *sg = uint8_t((*sg & ~(0xFu << sh)) | (((sw >> (16 * (c & 1) + 4 * k)) & 0xFu) << sh));
+                }
+            }
+        }
+        for (int r = 0; r < 16; ++r) {
+            copy_bytes(raw + r * row_bytes + gi * 110, in + 1664 + 2 * r, 2);
+            copy_bytes(raw + r * row_bytes + gi * 110 + 106, in + 1696 + 4 * r, 4);
+        }
+        return;
+    }
     if (type == T_IQ4_XS) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;

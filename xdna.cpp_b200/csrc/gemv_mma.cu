@@ -1,4 +1,4 @@
-// Integer tensor-core GEMV for Q4_0, Q3_K, Q4_K, Q5_K, Q6_K and IQ4_XS on sm_100a.
+// Integer tensor-core GEMV for Q4_0, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_XS and IQ3_S on sm_100a.
 //
 // Why tensor cores for an M = 1 GEMV: the contraction is bandwidth bound, but
 // unpacking and multiplying 4-bit weights on the FP32 pipes costs ~4
@@ -274,7 +274,9 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 template <int TYPE>
 constexpr int kUnitBytes =
     TYPE == T_Q5_K ? 2816
-                   : (TYPE == T_Q6_K ? 3360 : (TYPE == T_Q3_K ? 1760 : (TYPE == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
+                   : (TYPE == T_Q6_K ? 3360
+                                     : ((TYPE == T_Q3_K || TYPE == T_IQ3_S) ? 1760
+                                                                            : (TYPE == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
 template <int TYPE>
 constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
 template <int TYPE>
@@ -522,6 +524,64 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
     y8 = fmaf(h2f(h8.x), fmaf(k6[1][0] * sc2.x, T[2], k6[1][1] * sc2.y * T[3]), y8);
 }
 
+// IQ3_S: value = d * (1 + 2 s) * grid[idx] * sign with a 4-bit s per 32
+// values (ggml-quants.c dequantize_row_iq3_s).  Each A register is one grid
+// entry (4 unsigned magnitudes 1..15) read from the CTA's shared copy of the
+// 512-entry grid, with its 4 sign bits applied per byte: the bits are spread
+// to the bytes' top bits by a multiply, prmt's sign-replicate mode widens
+// them to 0x00 / 0xFF masks m, and (g ^ m) + (m & 1) negates the masked bytes
+// (no carry between bytes: every magnitude is at least 1).
+__shared__ uint32_t s_iq3s_grid[512];
+
+__device__ __forceinline__ uint32_t iq3s_reg(uint32_t iw, uint32_t hw, uint32_t sw, int k) {
+    const uint32_t idx = ((iw >> (8 * k)) & 0xFFu) | (((hw >> k) & 1u) << 8);
+    const uint32_t g = s_iq3s_grid[idx];
+    const uint32_t m = prmt(((sw >> (4 * k)) & 0xFu) * 0x10204080u, 0u, 0xBA98u);
+    return (g ^ m) + (m & 0x01010101u);
+}
+
+__device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t* fb, int fc,
+                                               const float* __restrict__ sc_, int lane, int g, int t, float& y0,
+                                               float& y8) {
+    const uint4 I0 = ld_stream(gb + lane * 32), I1 = ld_stream(gb + lane * 32 + 16);
+    const uint4 S = ld_stream(gb + 1024 + lane * 16);
+    const uint32_t qh = __ldg(reinterpret_cast<const unsigned int*>(gb + 1536) + lane);
+    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + g));
+    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + g + 8));
+    const uint32_t sg = __ldg(reinterpret_cast<const unsigned int*>(gb + 1696) + g);
+    const uint32_t s8 = __ldg(reinterpret_cast<const unsigned int*>(gb + 1696) + g + 8);
+    int C[3][4];
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
+        const uint32_t sw = word(S, c >> 1) >> (16 * (c & 1));
+        const uint32_t hw = qh >> (4 * c);
+        const uint32_t a0 = iq3s_reg(iw, hw, sw, 0), a1 = iq3s_reg(iw, hw, sw, 1);
+        const uint32_t a2 = iq3s_reg(iw, hw, sw, 2), a3 = iq3s_reg(iw, hw, sw, 3);
+        mma_s8s8(C[0], a0, a1, a2, a3, q.x, q.y);
+        mma_s8s8(C[1], a0, a1, a2, a3, q.z, q.w);
+        mma_s8s8(C[2], a0, a1, a2, a3, r.x, r.y);
+    }
+    // |sum| <= 32 * 15 * 2^23 passes 2^31: join the planes in F32
+    float T[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
+    // scales of blocks 2t (low nibble) and 2t + 1 (high nibble) are byte t of the row's scales
+    const uint32_t bg = (sg >> (8 * t)) & 0xFFu, b8 = (s8 >> (8 * t)) & 0xFFu;
+    const float kg0 = static_cast<float>(1 + 2 * (bg & 0xFu)), kg1 = static_cast<float>(1 + 2 * (bg >> 4));
+    const float k80 = static_cast<float>(1 + 2 * (b8 & 0xFu)), k81 = static_cast<float>(1 + 2 * (b8 >> 4));
+    y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
+    y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
+}
+
 // Q4_0, Q4_K, Q5_K: one set of 8 thirty-two-value blocks, 4- or 5-bit q.
 template <int TYPE>
 __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* fb, int fc,
@@ -630,6 +690,8 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         group_dot_q3k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ4_XS)
         group_dot_iq4xs(gb, fb, fc, sc_, lane, g, t, y0, y8);
+    else if constexpr (TYPE == T_IQ3_S)
+        group_dot_iq3s(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else
         group_dot_nib<TYPE>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
@@ -674,6 +736,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     const int t0 = kTiles ? sp.cta_unit0(static_cast<int>(blockIdx.x)) / ng
                           : static_cast<int>(int64_t(blockIdx.x) * kWarps * U / NW) / ng;
     for (int i = threadIdx.x; i < a.cta_tiles; i += blockDim.x) s_count[i] = 0;
+    if constexpr (TYPE == T_IQ3_S)
+        for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
     __syncthreads();
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
@@ -1065,7 +1129,7 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
-    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K || type == T_IQ4_XS) {
+    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K || type == T_IQ4_XS || type == T_IQ3_S) {
         const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
         if (pack)
             mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
@@ -1093,6 +1157,7 @@ static cudaError_t launch_gemv(int type, cudaLaunchConfig_t& cg, const GemvArgs&
         case T_Q6_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q6_K, kTiles>, a);
         case T_Q3_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q3_K, kTiles>, a);
         case T_IQ4_XS: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ4_XS, kTiles>, a);
+        case T_IQ3_S: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ3_S, kTiles>, a);
         default: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0, kTiles>, a);
     }
 }
@@ -1107,7 +1172,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg,
                                   const MmaFeed* feed, bool x_ready) {
     if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K &&
-         type != T_IQ4_XS) ||
+         type != T_IQ4_XS && type != T_IQ3_S) ||
         nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
