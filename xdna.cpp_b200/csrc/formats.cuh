@@ -392,27 +392,46 @@ constexpr int MMA_GROUP_BYTES = 2304;  // Q4_0 / Q4_K group (16 rows x 144 B)
 //                register's 4 sign bits, in value order;
 //   [1536, 1664) per lane 4 B: bit 4 c + k = the entry's index bit 8;
 //   [1664, 1696) the 16 rows' fp16 d;  [1696, 1760) the 16 rows' scales[4].
+//
+// IQ3_XXS (8-bit indices into the 256-entry grid, one per 4 values; per 8
+// values a 7-bit sign index whose 8th sign makes the count even; 4-bit scales
+// per 32): register k of chunk c is grid entry 8 (block) + c:
+//   [0, 1024)    per lane 32 B: word c, byte k = the entry's grid index;
+//   [1024, 1536) per lane 16 B: word p (chunk pair 2p, 2p + 1), bits 7 k .. + 6
+//                = the pair's 7-bit sign index for register k; bits 28-31 = the
+//                scale of (row g + 8 (p % 2), block 2t + p / 2);
+//   [1536, 1568) the 16 rows' fp16 d.
+//
+// IQ2_S (10-bit indices into the 1024-entry grid, one per 8 values; a sign
+// bit per value; 4-bit scales per 16): 16-value x blocks as Q6_K; chunks 2q
+// and 2q + 1 of register k share one grid entry (low and high 4 values):
+//   [0, 512)     per lane 16 B: byte 4 q + k = the entry's low index byte;
+//   [512, 1024)  per lane 16 B: byte 4 q + k = the entry's 8 sign bits;
+//   [1024, 1152) per lane 4 B: bits 2 (4 q + k) .. + 1 = the index bits 8-9;
+//   [1152, 1280) per lane 4 B: nibble 4 st + 2 h + b = the scale of row g + 8 h,
+//                16-value block 8 st + 2 t + b;
+//   [1280, 1312) the 16 rows' fp16 d.
 XB_HD int mma_group_bytes(int type) {
-    return type == T_Q5_K ? 2816
-                          : (type == T_Q6_K ? 3360
-                                            : ((type == T_Q3_K || type == T_IQ3_S) ? 1760
-                                                                                    : (type == T_IQ4_XS ? 2176
-                                                                                                        : MMA_GROUP_BYTES)));
+    switch (type) {
+        case T_Q5_K: return 2816;
+        case T_Q6_K: return 3360;
+        case T_Q3_K:
+        case T_IQ3_S: return 1760;
+        case T_IQ4_XS: return 2176;
+        case T_IQ3_XXS: return 1568;
+        case T_IQ2_S: return 1312;
+        default: return MMA_GROUP_BYTES;
+    }
 }
 XB_HD int mma_header_off(int type) { return type == T_Q5_K ? 2560 : (type == T_Q6_K ? 3072 : 2048); }
 // GGUF bytes of one row's 256-value group (8 Q4_0 blocks or one K super-block)
-XB_HD int mma_row_group_bytes(int type) {
-    return type == T_Q5_K ? 176
-                          : (type == T_Q6_K ? 210
-                                            : ((type == T_Q3_K || type == T_IQ3_S) ? 110
-                                                                                    : (type == T_IQ4_XS ? 136 : 144)));
-}
+XB_HD int mma_row_group_bytes(int type) { return mma_group_bytes(type) / MMA_TILE_ROWS; }
 // x blocks (B columns) of 16 values instead of 32
-XB_HD bool mma_blk16(int type) { return type == T_Q6_K || type == T_Q3_K; }
+XB_HD bool mma_blk16(int type) { return type == T_Q6_K || type == T_Q3_K || type == T_IQ2_S; }
 
 XB_HD int layout_kind(int type, int64_t N, int64_t K) {
     return ((type == T_Q4_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q3_K ||
-             type == T_IQ4_XS || type == T_IQ3_S) &&
+             type == T_IQ4_XS || type == T_IQ3_S || type == T_IQ3_XXS || type == T_IQ2_S) &&
             N > 0 && K > 0 && N % MMA_TILE_ROWS == 0 && K % 256 == 0)
                ? 1
                : 0;
@@ -510,7 +529,60 @@ XB_HD uint8_t* iq3s_qs(uint8_t* row, int64_t gi, int e) { return row + gi * 110 
 XB_HD uint8_t* iq3s_qh(uint8_t* row, int64_t gi, int e) { return row + gi * 110 + 66 + (e >> 3); }
 XB_HD uint8_t* iq3s_sg(uint8_t* row, int64_t gi, int e) { return row + gi * 110 + 74 + (e >> 1); }
 
+// IQ3_XXS block bytes: d, qs[64], then 8 words (4 x 7-bit sign index | scale << 28)
+XB_HD uint8_t* iq3xxs_word(uint8_t* row, int64_t gi, int blk) { return row + gi * 98 + 66 + 4 * blk; }
+// IQ2_S block bytes: d, qs[32], signs[32], qh[8], scales[8]; entry e covers values 8e .. 8e + 7
+XB_HD uint8_t* iq2s_at(uint8_t* row, int64_t gi, int off) { return row + gi * 82 + off; }
+
 XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64_t gi, uint8_t* out) {
+    uint8_t* rw = const_cast<uint8_t*>(raw);
+    if (type == T_IQ3_XXS) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c)
+                for (int k = 0; k < 4; ++k)
+                    out[lane * 32 + 4 * c + k] =
+                        *(rw + (g + 8 * (k & 1)) * row_bytes + gi * 98 + 2 + 8 * (t + 4 * (k >> 1)) + c);
+            for (int p = 0; p < 4; ++p) {
+                uint32_t w = 0;
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t aux = get32(iq3xxs_word(rw + (g + 8 * (k & 1)) * row_bytes, gi, t + 4 * (k >> 1)));
+                    w |= ((aux >> (7 * p)) & 127u) << (7 * k);
+                }
+                const uint32_t aux = get32(iq3xxs_word(rw + (g + 8 * (p & 1)) * row_bytes, gi, 2 * t + (p >> 1)));
+                w |= aux & 0xF0000000u;
+                put32(out + 1024 + lane * 16 + 4 * p, w);
+            }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(out + 1536 + 2 * r, raw + r * row_bytes + gi * 98, 2);
+        return;
+    }
+    if (type == T_IQ2_S) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            uint32_t hw = 0, sw = 0;
+            for (int q = 0; q < 4; ++q)
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = rw + (g + 8 * (k & 1)) * row_bytes;
+                    const int e = 2 * (8 * (q >> 1) + t + 4 * (k >> 1)) + (q & 1);
+                    out[lane * 16 + 4 * q + k] = *iq2s_at(row, gi, 2 + e);
+                    out[512 + lane * 16 + 4 * q + k] = *iq2s_at(row, gi, 34 + e);
+                    hw |= ((static_cast<uint32_t>(*iq2s_at(row, gi, 66 + (e >> 2))) >> (2 * (e & 3))) & 3u)
+                          << (2 * (4 * q + k));
+                }
+            for (int st = 0; st < 2; ++st)
+                for (int h = 0; h < 2; ++h)
+                    for (int b = 0; b < 2; ++b) {
+                        const int B = 8 * st + 2 * t + b;
+                        const uint32_t sc = *iq2s_at(rw + (g + 8 * h) * row_bytes, gi, 74 + (B >> 1));
+                        sw |= ((sc >> (4 * (B & 1))) & 0xFu) << (4 * (4 * st + 2 * h + b));
+                    }
+            put32(out + 1024 + lane * 4, hw);
+            put32(out + 1152 + lane * 4, sw);
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(out + 1280 + 2 * r, raw + r * row_bytes + gi * 82, 2);
+        return;
+    }
     if (type == T_IQ3_S) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;
@@ -669,6 +741,53 @@ XB_HD void mma_pack_group(int type, const uint8_t* raw, int64_t row_bytes, int64
 }
 
 XB_HD void mma_unpack_group(int type, const uint8_t* in, int64_t row_bytes, int64_t gi, uint8_t* raw) {
+    if (type == T_IQ3_XXS) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            for (int c = 0; c < 8; ++c)
+                for (int k = 0; k < 4; ++k)
+                    *(raw + (g + 8 * (k & 1)) * row_bytes + gi * 98 + 2 + 8 * (t + 4 * (k >> 1)) + c) =
+                        in[lane * 32 + 4 * c + k];
+            for (int p = 0; p < 4; ++p) {
+                const uint32_t w = get32(in + 1024 + lane * 16 + 4 * p);
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* a = iq3xxs_word(raw + (g + 8 * (k & 1)) * row_bytes, gi, t + 4 * (k >> 1));
+                    const uint32_t m = 127u << (7 * p);
+                    put32(a, (get32(a) & ~m) | (((w >> (7 * k)) & 127u) << (7 * p)));
+                }
+                uint8_t* a = iq3xxs_word(raw + (g + 8 * (p & 1)) * row_bytes, gi, 2 * t + (p >> 1));
+                put32(a, (get32(a) & 0x0FFFFFFFu) | (w & 0xF0000000u));
+            }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 98, in + 1536 + 2 * r, 2);
+        return;
+    }
+    if (type == T_IQ2_S) {
+        for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            const uint32_t hw = get32(in + 1024 + lane * 4), sw = get32(in + 1152 + lane * 4);
+            for (int q = 0; q < 4; ++q)
+                for (int k = 0; k < 4; ++k) {
+                    uint8_t* row = raw + (g + 8 * (k & 1)) * row_bytes;
+                    const int e = 2 * (8 * (q >> 1) + t + 4 * (k >> 1)) + (q & 1);
+                    *iq2s_at(row, gi, 2 + e) = in[lane * 16 + 4 * q + k];
+                    *iq2s_at(row, gi, 34 + e) = in[512 + lane * 16 + 4 * q + k];
+                    uint8_t* h = iq2s_at(row, gi, 66 + (e >> 2));
+                    const int sh = 2 * (e & 3);
+                    *h = uint8_t((*h & ~(3u << sh)) | (((hw >> (2 * (4 * q + k))) & 3u) << sh));
+                }
+            for (int st = 0; st < 2; ++st)
+                for (int h = 0; h < 2; ++h)
+                    for (int b = 0; b < 2; ++b) {
+                        const int B = 8 * st + 2 * t + b;
+                        uint8_t* sc = iq2s_at(raw + (g + 8 * h) * row_bytes, gi, 74 + (B >> 1));
+                        const int sh = 4 * (B & 1);
+                        *sc = uint8_t((*sc & ~(0xFu << sh)) | (((sw >> (4 * (4 * st + 2 * h + b))) & 0xFu) << sh));
+                    }
+        }
+        for (int r = 0; r < 16; ++r) copy_bytes(raw + r * row_bytes + gi * 82, in + 1280 + 2 * r, 2);
+        return;
+    }
     if (type == T_IQ3_S) {
         for (int lane = 0; lane < 32; ++lane) {
             const int g = lane >> 2, t = lane & 3;

@@ -1,4 +1,5 @@
-// Integer tensor-core GEMV for Q4_0, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_XS and IQ3_S on sm_100a.
+// Integer tensor-core GEMV for all nine claimed formats on sm_100a: Q4_0, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_XS,
+// IQ3_S, IQ3_XXS and IQ2_S.
 //
 // Why tensor cores for an M = 1 GEMV: the contraction is bandwidth bound, but
 // unpacking and multiplying 4-bit weights on the FP32 pipes costs ~4
@@ -275,12 +276,16 @@ template <int TYPE>
 constexpr int kUnitBytes =
     TYPE == T_Q5_K ? 2816
                    : (TYPE == T_Q6_K ? 3360
-                                     : ((TYPE == T_Q3_K || TYPE == T_IQ3_S) ? 1760
-                                                                            : (TYPE == T_IQ4_XS ? 2176 : MMA_GROUP_BYTES)));
+                                     : ((TYPE == T_Q3_K || TYPE == T_IQ3_S)
+                                            ? 1760
+                                            : (TYPE == T_IQ4_XS ? 2176
+                                                                : (TYPE == T_IQ3_XXS ? 1568
+                                                                                     : (TYPE == T_IQ2_S ? 1312
+                                                                                                        : MMA_GROUP_BYTES)))));
 template <int TYPE>
 constexpr int kHeaderOff = TYPE == T_Q5_K ? 2560 : 2048;
 template <int TYPE>
-constexpr int kXBlocks = (TYPE == T_Q6_K || TYPE == T_Q3_K) ? 16 : 8;  // x blocks (scales, sums) per 256 values
+constexpr int kXBlocks = (TYPE == T_Q6_K || TYPE == T_Q3_K || TYPE == T_IQ2_S) ? 16 : 8;  // x blocks per 256 values
 
 template <int TYPE>
 __device__ __forceinline__ const uint8_t* unit_weights(const GemvArgs& a, int64_t u) {
@@ -533,11 +538,14 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
 // (no carry between bytes: every magnitude is at least 1).
 __shared__ uint32_t s_iq3s_grid[512];
 
+// four unsigned magnitudes g (each >= 1) with 4 sign bits applied, as s8
+__device__ __forceinline__ uint32_t signed4(uint32_t g, uint32_t s4) {
+    const uint32_t m = prmt(s4 * 0x10204080u, 0u, 0xBA98u);
+    return (g ^ m) + (m & 0x01010101u);
+}
 __device__ __forceinline__ uint32_t iq3s_reg(uint32_t iw, uint32_t hw, uint32_t sw, int k) {
     const uint32_t idx = ((iw >> (8 * k)) & 0xFFu) | (((hw >> k) & 1u) << 8);
-    const uint32_t g = s_iq3s_grid[idx];
-    const uint32_t m = prmt(((sw >> (4 * k)) & 0xFu) * 0x10204080u, 0u, 0xBA98u);
-    return (g ^ m) + (m & 0x01010101u);
+    return signed4(s_iq3s_grid[idx], (sw >> (4 * k)) & 0xFu);
 }
 
 __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t* fb, int fc,
@@ -580,6 +588,119 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
     const float k80 = static_cast<float>(1 + 2 * (b8 & 0xFu)), k81 = static_cast<float>(1 + 2 * (b8 >> 4));
     y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
     y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
+}
+
+// IQ3_XXS: value = d * (0.5 + s) / 2 * grid[q] * sign with a 4-bit s per 32
+// values (gguf quants.py IQ3_XXS).  As IQ3_S, one shared-memory grid entry
+// (256 entries, magnitudes 4..62) per A register; the 8 signs of 8 values
+// are a 7-bit index plus the bit that makes the count of negatives even.
+__shared__ uint32_t s_iq3xxs_grid[256];
+
+__device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_t* fb, int fc,
+                                                 const float* __restrict__ sc_, int lane, int g, int t, float& y0,
+                                                 float& y8) {
+    const uint4 I0 = ld_stream(gb + lane * 32), I1 = ld_stream(gb + lane * 32 + 16);
+    const uint4 SS = ld_stream(gb + 1024 + lane * 16);
+    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1536) + g));
+    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1536) + g + 8));
+    int C[3][4];
+#pragma unroll
+    for (int p = 0; p < 3; ++p)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
+        const uint32_t w = word(SS, c >> 1);
+        uint32_t a[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t si = (w >> (7 * k)) & 127u;
+            const uint32_t sb = si | ((__popc(si) & 1u) << 7);
+            a[k] = signed4(s_iq3xxs_grid[(iw >> (8 * k)) & 0xFFu], (sb >> (4 * (c & 1))) & 0xFu);
+        }
+        mma_s8s8(C[0], a[0], a[1], a[2], a[3], q.x, q.y);
+        mma_s8s8(C[1], a[0], a[1], a[2], a[3], q.z, q.w);
+        mma_s8s8(C[2], a[0], a[1], a[2], a[3], r.x, r.y);
+    }
+    // |sum| <= 32 * 62 * 2^23 passes 2^31: join the planes in F32
+    float T[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
+    // scales (top nibble of word p): p = 0 (g, 2t), 1 (g+8, 2t), 2 (g, 2t+1), 3 (g+8, 2t+1)
+    const float kg0 = 0.5f * (0.5f + static_cast<float>(SS.x >> 28));
+    const float k80 = 0.5f * (0.5f + static_cast<float>(SS.y >> 28));
+    const float kg1 = 0.5f * (0.5f + static_cast<float>(SS.z >> 28));
+    const float k81 = 0.5f * (0.5f + static_cast<float>(SS.w >> 28));
+    y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
+    y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
+}
+
+// IQ2_S: value = d * (0.5 + s) / 4 * grid[q] * sign with a 4-bit s per 16
+// values (gguf quants.py IQ2_S); two sets of 8 sixteen-value blocks as Q6_K.
+// A grid entry (1024 entries of 8 magnitudes 8..43, shared memory) covers
+// chunks 2q and 2q + 1 of one register: one 64-bit load feeds two registers.
+__shared__ unsigned long long s_iq2s_grid[1024];
+
+__device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t* fb, int fc,
+                                               const float* __restrict__ sc_, int lane, int g, int t, float& y0,
+                                               float& y8) {
+    const uint4 IL = ld_stream(gb + lane * 16);
+    const uint4 SG = ld_stream(gb + 512 + lane * 16);
+    const uint32_t qh = __ldg(reinterpret_cast<const unsigned int*>(gb + 1024) + lane);
+    const uint32_t scw = __ldg(reinterpret_cast<const unsigned int*>(gb + 1152) + lane);
+    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1280) + g));
+    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1280) + g + 8));
+#pragma unroll
+    for (int st = 0; st < 2; ++st) {
+        int C[3][4];
+#pragma unroll
+        for (int p = 0; p < 3; ++p)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) C[p][k] = 0;
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+            const int q = 2 * st + qq;
+            const uint32_t il = word(IL, q), sg = word(SG, q);
+            uint32_t lo[4], hi[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t idx = ((il >> (8 * k)) & 0xFFu) | (((qh >> (2 * (4 * q + k))) & 3u) << 8);
+                const unsigned long long gv = s_iq2s_grid[idx];
+                const uint32_t sb = (sg >> (8 * k)) & 0xFFu;
+                lo[k] = signed4(static_cast<uint32_t>(gv), sb & 0xFu);
+                hi[k] = signed4(static_cast<uint32_t>(gv >> 32), sb >> 4);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int c = 4 * st + 2 * qq + h;
+                const uint4 bq = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
+                const uint2 br = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+                const uint32_t* a = h ? hi : lo;
+                mma_s8s8(C[0], a[0], a[1], a[2], a[3], bq.x, bq.y);
+                mma_s8s8(C[1], a[0], a[1], a[2], a[3], bq.z, bq.w);
+                mma_s8s8(C[2], a[0], a[1], a[2], a[3], br.x, br.y);
+            }
+        }
+        // |sum| <= 16 * 43 * 2^23 passes 2^31: join the planes in F32
+        float T[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
+        // nibble 4 st + 2 h + b: row g + 8 h, block 8 st + 2 t + b
+        const uint32_t n = scw >> (16 * st);
+        const float kg0 = 0.25f * (0.5f + static_cast<float>(n & 0xFu));
+        const float kg1 = 0.25f * (0.5f + static_cast<float>((n >> 4) & 0xFu));
+        const float k80 = 0.25f * (0.5f + static_cast<float>((n >> 8) & 0xFu));
+        const float k81 = 0.25f * (0.5f + static_cast<float>((n >> 12) & 0xFu));
+        y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
+        y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
+    }
 }
 
 // Q4_0, Q4_K, Q5_K: one set of 8 thirty-two-value blocks, 4- or 5-bit q.
@@ -692,6 +813,10 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         group_dot_iq4xs(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ3_S)
         group_dot_iq3s(gb, fb, fc, sc_, lane, g, t, y0, y8);
+    else if constexpr (TYPE == T_IQ3_XXS)
+        group_dot_iq3xxs(gb, fb, fc, sc_, lane, g, t, y0, y8);
+    else if constexpr (TYPE == T_IQ2_S)
+        group_dot_iq2s(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else
         group_dot_nib<TYPE>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
@@ -738,6 +863,10 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     for (int i = threadIdx.x; i < a.cta_tiles; i += blockDim.x) s_count[i] = 0;
     if constexpr (TYPE == T_IQ3_S)
         for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
+    if constexpr (TYPE == T_IQ3_XXS)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_iq3xxs_grid[i] = kIq3xxsGrid[i];
+    if constexpr (TYPE == T_IQ2_S)
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s_grid[i] = kIq2sGrid[i];
     __syncthreads();
     // start this warp's first weights towards L2 before waiting on xprep
     if (lane == 0)
@@ -1129,7 +1258,7 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
                               cudaStream_t stream) {
     if (layout_kind(type, N, K) != 1) return cudaErrorInvalidValue;
     const int64_t ntiles = N / MMA_TILE_ROWS, items = ntiles * (K / 256);
-    if (type == T_Q5_K || type == T_Q6_K || type == T_Q3_K || type == T_IQ4_XS || type == T_IQ3_S) {
+    if (type != T_Q4_0 && type != T_Q4_K) {  // every other MMA format: the per-group routine
         const int64_t blocks = (items + 127) / 128 < 65536 ? (items + 127) / 128 : 65536;
         if (pack)
             mma_repack_generic_kernel<true><<<unsigned(blocks), 128, 0, stream>>>(
@@ -1158,6 +1287,8 @@ static cudaError_t launch_gemv(int type, cudaLaunchConfig_t& cg, const GemvArgs&
         case T_Q3_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q3_K, kTiles>, a);
         case T_IQ4_XS: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ4_XS, kTiles>, a);
         case T_IQ3_S: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ3_S, kTiles>, a);
+        case T_IQ3_XXS: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ3_XXS, kTiles>, a);
+        case T_IQ2_S: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ2_S, kTiles>, a);
         default: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0, kTiles>, a);
     }
 }
@@ -1171,8 +1302,7 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg,
                                   const MmaFeed* feed, bool x_ready) {
-    if ((type != T_Q4_K && type != T_Q4_0 && type != T_Q5_K && type != T_Q6_K && type != T_Q3_K &&
-         type != T_IQ4_XS && type != T_IQ3_S) ||
+    if (layout_kind(type, MMA_TILE_ROWS, 256) != 1 ||
         nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
     if (xchg && (xchg->world < 2 || xchg->world > kMaxPeers || xchg->rank < 0 || xchg->rank >= xchg->world))
