@@ -3,7 +3,9 @@
  *
  * The library claims single-row (M = 1) GGML_OP_MUL_MAT with Q4_0, Q3_K, Q4_K,
  * Q5_K, Q6_K, IQ2_S, IQ3_S, IQ3_XXS or IQ4_XS weights and F32 activations and
- * runs it as hand-written sm_100a dequant-GEMV kernels.
+ * runs it as hand-written sm_100a kernels: an integer tensor-core GEMV for
+ * every format (matrices of 16-row tiles), an F32 dequantise-and-FMA kernel
+ * for the other row counts.
  *
  * Section 1 is the reference's ggml-free "backwards-compatibility" C ABI with
  * the same names, argument meaning and error behaviour

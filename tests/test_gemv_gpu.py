@@ -304,10 +304,11 @@ def test_concurrent_threads_share_a_backend(cuda, G, O):
 
 
 def test_mma_split_shapes_interleaved_and_deterministic(cuda, G, O):
-    """The 4-bit MMA path splits K into slices and tiles across warps, with
-    per-tile arrival counters that every launch must leave at zero: shapes
-    that share one stream's scratch, interleaved, give the oracle's result
-    each time and identical bits on repeats (fixed summation order)."""
+    """The MMA path splits K into slices and tiles across warps (unit mode)
+    or whole tiles across CTAs (tile mode), with per-tile arrival counters
+    that every launch must find cleared: shapes that share one stream's
+    scratch, interleaved, give the oracle's result each time and identical
+    bits on repeats (fixed summation order)."""
     cases = [(G.Q4_K, 2048, 256 * 43), (G.Q4_0, 1024, 5120), (G.Q4_K, 64, 512), (G.Q4_K, 4096, 256 * 42),
              (G.Q4_0, 16, 256), (G.Q4_K, 16384, 2048)]
     data = []

@@ -1,6 +1,6 @@
 """b200_gemv_noalloc: the GEMV entry point that allocates no device memory.
 
-It must give what b200_gemv gives (same kernels; the 4-bit MMA path with its
+It must give what b200_gemv gives (same kernels; the MMA path with its
 scratch in a fixed static device array), on consecutive calls, whether this
 file runs alone or after the rest of the suite, and reject shapes whose
 scratch would not fit the array.  Collected last on purpose (file name).
