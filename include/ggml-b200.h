@@ -120,7 +120,7 @@ const char *ggml_backend_xdna_buft_name(ggml_backend_buffer_type_t buft);
 ggml_backend_buffer_t ggml_backend_xdna_buft_alloc_buffer(ggml_backend_buffer_type_t buft, size_t size);
 /* Alignment of tensor data offsets inside a buffer: 4096 (reference :407-410). */
 size_t ggml_backend_xdna_buft_get_alignment(ggml_backend_buffer_type_t buft);
-/* Bytes a tensor occupies: ggml_nbytes; the stripe layout has the same span (reference :417-454). */
+/* Bytes a tensor occupies: ggml_nbytes; both device layouts have the same span (reference :417-454). */
 size_t ggml_backend_xdna_buft_get_alloc_size(ggml_backend_buffer_type_t buft, const struct ggml_tensor_xdna *tensor);
 /* false for the device type, true for the host type (reference :456-459 returns true). */
 bool ggml_backend_xdna_buft_is_host(ggml_backend_buffer_type_t buft);
@@ -130,7 +130,8 @@ void *ggml_backend_xdna_buffer_get_base(ggml_backend_buffer_t buffer);
 size_t ggml_backend_xdna_buffer_get_size(ggml_backend_buffer_t buffer);
 /* Host -> tensor bytes [offset, offset + size) in GGUF layout (reference
  * buf_set_tensor :341-345).  Quantised weight tensors are uploaded through a
- * bounded pinned staging ring and repacked on the GPU into the stripe layout. */
+ * bounded pinned staging ring and repacked on the GPU into the device layout
+ * (MMA tiles or stripe tiles, as b200_gemv describes). */
 bool ggml_backend_xdna_buffer_set_tensor(ggml_backend_buffer_t buffer, struct ggml_tensor_xdna *tensor,
                                          const void *data, size_t offset, size_t size);
 /* Tensor -> host, GGUF layout (reference buf_get_tensor :347-351). */
@@ -159,14 +160,17 @@ size_t ggml_backend_xdna_get_device_count(void);
 /* ===================== 3. launcher layer (device pointers) ===================== */
 
 /* y[N] = W[N,K] x[K] on `stream` (a cudaStream_t, NULL = legacy default).  W is
- * in the stripe layout (see b200_repack).  x must be 16-byte aligned.  pdl != 0
+ * in the device layout b200_repack writes: 16-row MMA tiles for every format
+ * when N % 16 == 0 and K % 256 == 0, stripe tiles otherwise.  x must be
+ * 16-byte aligned.  pdl != 0
  * launches with programmatic dependent launch.  Replaces the reference's
  * XdnaGemvEngine::run / run_quant (src/xdna-gemv-engine.cpp:1817-1992). */
 int b200_gemv(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
               void *stream, int pdl);
 /* y_s = W_s x for up to 4 matrices that share x (q / k / v or gate / up of a
  * transformer block) in one x preparation and one GEMV launch.  Every W_s must
- * be in the 16-row MMA layout (Q4_0 / Q4_K, N_s % 16 == 0, K % 256 == 0).  No
+ * be in the 16-row MMA layout (any of the nine formats, N_s % 16 == 0,
+ * K % 256 == 0).  No
  * reference counterpart; ggml_backend_xdna_compute_graph applies the same
  * fusion to consecutive nodes that qualify. */
 int b200_gemv_multi(int type, const void *const *w_packed, float *const *y, const int64_t *n, int nseg,
@@ -176,17 +180,19 @@ int b200_gemv_multi(int type, const void *const *w_packed, float *const *y, cons
  * cannot allocate device memory at call time: a host that has handed all
  * device memory to its own pools, or a decode loop that cannot take the
  * device-wide synchronisation of cudaMalloc / cudaFree in the middle of a
- * token.  The Q4_0 / Q4_K MMA path (N % 16 == 0, K % 256 == 0) then uses a
- * fixed 1 MiB static device array for its scratch instead of the per-stream
- * buffers b200_gemv grows on demand; shapes needing more (above N = 131072
- * with K = 32768) fail with an error naming the limit.  The other formats
- * need no scratch and run as in b200_gemv.  The array's device address is
+ * token.  The MMA path, which every format takes when N % 16 == 0 and
+ * K % 256 == 0, then uses a fixed 1 MiB static device array for its scratch
+ * instead of the per-stream buffers b200_gemv grows on demand; shapes needing
+ * more (above N = 131072 with K = 32768) fail with an error naming the limit.
+ * Matrices in the stripe layout (N % 16 != 0) need no scratch and run as in
+ * b200_gemv.  The array's device address is
  * looked up (cudaGetSymbolAddress) by the first call on each device, so make
  * that first call before capturing a stream.  The array is shared by every
  * stream of the device: calls whose executions overlap in time race. */
 int b200_gemv_noalloc(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
                       void *stream);
-/* GGUF rows -> stripe layout (out of place), the GPU replacement of the
+/* GGUF rows -> device layout (MMA tiles or stripe tiles, as b200_gemv
+ * describes; out of place), the GPU replacement of the
  * reference's Q4Prepacker::pack (src/xdna-q4-prepack.cpp:39-114). */
 int b200_repack(int type, const void *raw, void *packed, int64_t n, int64_t k, void *stream);
 /* Inverse of b200_repack (Q4Prepacker::dequantize_packed's role, exact). */

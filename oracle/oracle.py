@@ -35,8 +35,10 @@ _u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 
 
-def build(ref_dir: str = "/root/reference") -> None:
-    """Compile the oracle (and, where the reference tree exists, oracle/_ref)."""
+def build(ref_dir: str | None = None) -> None:
+    """Compile the oracle (and oracle/_ref when the reference tree is given,
+    by argument or by the XDNA_REFERENCE_DIR environment variable)."""
+    ref_dir = ref_dir if ref_dir is not None else os.environ.get("XDNA_REFERENCE_DIR", "")
     subprocess.run(["make", "-C", HERE, f"REF_DIR={ref_dir}", "all"], check=True,
                    stdout=subprocess.DEVNULL)
 

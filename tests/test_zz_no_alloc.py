@@ -12,9 +12,13 @@ from helpers import check_parity, normal_weights, normal_x, to_dev
 
 pytestmark = pytest.mark.gpu
 
-# (type, N, K): MMA path with K slices of 8 groups, MMA path with a K that is
-# not a multiple of 8 groups, a tall MMA matrix, and a stripe-layout format
-CASES = [("Q4_K", 4096, 4096), ("Q4_0", 2048, 5120), ("Q4_K", 16384, 2048), ("Q6_K", 256, 1024)]
+# (type, N, K): every format takes the MMA path (scratch in the static array)
+# when N % 16 == 0 and K % 256 == 0: Q4_K and Q4_0 (32-value x blocks), a
+# tall Q4_K matrix, Q6_K (16-value x blocks) and IQ2_S (grid decode, 16-value
+# x blocks).  N % 16 != 0 takes the stripe layout, which needs no scratch
+# (Q4_K with N = 4104).
+CASES = [("Q4_K", 4096, 4096), ("Q4_0", 2048, 5120), ("Q4_K", 16384, 2048), ("Q6_K", 256, 1024),
+         ("IQ2_S", 4096, 4096), ("Q4_K", 4104, 2048)]
 
 
 @pytest.mark.parametrize("name,N,K", CASES)

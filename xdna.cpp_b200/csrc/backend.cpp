@@ -1709,7 +1709,7 @@ int b200_gemv_multi(int type, const void* const* w_packed, float* const* y, cons
     for (int s = 0; s < nseg; ++s) {
         if (!w_packed[s] || !y[s] || layout_kind(type, n[s], k) != 1) {
             set_error("b200_gemv_multi: matrix %d (type %d, N=%ld, K=%ld) is not in the 16-row MMA layout "
-                      "(Q4_0 / Q4_K, N %% 16 == 0, K %% 256 == 0)",
+                      "(N %% 16 == 0 and K %% 256 == 0)",
                       s, type, long(n[s]), long(k));
             return -1;
         }

@@ -38,7 +38,6 @@ constexpr int kItemRows = 2;  // rows per warp work item (x reuse factor)
 static_assert(TILE_ROWS % kItemRows == 0, "items must not straddle tiles");
 constexpr int kWarps = kThreads / 32;
 constexpr float kMagic = 8388608.0f;  // 2^23
-constexpr int kMaxDevices = 16;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -6,6 +6,9 @@
 
 namespace xb {
 
+// Devices a process may use with the per-device caches of this library.
+constexpr int kMaxDevices = 64;
+
 // A launch whose output segment `seg` is, in full, the x of the launch that
 // follows it on the stream: its epilogue writes that x's digit fragments,
 // scales and sums into the next launch's scratch (next_scratch, sized by

@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "formats.cuh"
@@ -1015,11 +1016,12 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
 }
 
 // Peers' rows -> the full outputs, after every peer's flag reached `epoch`.
-// Launched with programmatic dependent launch: it waits on the peers' flags
-// while this GPU's GEMV drains, then (griddepcontrol.wait) on that GEMV before
-// finishing, so the next kernel sees both halves of every output.  The flag
-// wait is bounded (1 s of %globaltimer); on time-out *err is set and nothing
-// is copied, so the host reports an error instead of the GPU hanging.
+// Launched with programmatic dependent launch: it first waits
+// (griddepcontrol.wait) for this GPU's GEMV to complete, which also makes the
+// GEMV's stored epoch visible, then polls the peers' flags, so the next kernel
+// sees both halves of every output.  The flag wait is bounded (1 s of
+// %globaltimer); on time-out *err is set and nothing is copied, so the host
+// reports an error instead of the GPU hanging.
 constexpr uint64_t kGatherWaitNs = 1000000000ull;  // 1 s of %globaltimer
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -1212,6 +1214,21 @@ int g_scratch_n = 0;
 
 }  // namespace
 
+// SM count of the current device, looked up once per device.  Entries are
+// atomics, so launcher threads that race on the first lookup of a device
+// store the same value without a data race.
+static int sm_count() {
+    static std::atomic<int> sms[kMaxDevices];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    int v = sms[dev].load(std::memory_order_relaxed);
+    if (v == 0) {
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) return -1;
+        sms[dev].store(v, std::memory_order_relaxed);
+    }
+    return v;
+}
+
 // Counters of a launch over `ntiles` tiles: one per tile, the CTA completion
 // counter, and one per 32-value chunk of an output that feeds the next launch.
 // All start at zero: cleared by the x-preparation kernel, or by the launch
@@ -1356,12 +1373,8 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     }
     if (a.units >= (int64_t(1) << 31)) return cudaErrorInvalidValue;  // the kernel counts units in 32 bits
 
-    static int s_sms[16] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
-    if (s_sms[dev] == 0) cudaDeviceGetAttribute(&s_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    const int sms = s_sms[dev] > 0 ? s_sms[dev] : 148;
+    const int sms = sm_count();
+    if (sms <= 0) return cudaErrorInvalidDevice;
     int64_t blocks = int64_t(sms) * kCtasPerSm;
     if (blocks > kMaxCtas) blocks = kMaxCtas;
     // Tile mode up to 64 units per SM: at 11008 x 2048 it lifted the formats
@@ -1484,11 +1497,11 @@ size_t static_scratch_bytes() { return sizeof(g_static_scratch); }
 // per device (cudaGetSymbolAddress) and cached.
 cudaError_t static_scratch(void** out) {
     static std::mutex m;
-    static void* addr[64] = {};
+    static void* addr[kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(m);
     if (!addr[dev]) {
         void* p = nullptr;
