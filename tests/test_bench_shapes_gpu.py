@@ -151,3 +151,20 @@ def test_ne2_ne3_loop(cuda, G, O, resident):
                 check_parity(Y[i], O.gemv(t, mats[i], N, K, x), f"slice {i} broadcast={broadcast}")
         if buf is not None:
             buf.free()
+
+
+@pytest.mark.parametrize("name,N,K", [("Q4_K", 256, 8192), ("Q4_K", 40, 1024), ("IQ2_S", 256, 4096),
+                                      ("Q4_0", 512, 4096)])
+@pytest.mark.parametrize("bad", [float("nan"), float("inf")])
+def test_nonfinite_activations_propagate(cuda, G, O, name, N, K, bad):
+    """An infinity or a NaN in x reaches every output row as a non-finite
+    value, as in the reference's F32 dot products (the integer path carries
+    it through the block scale); the other blocks' values do not hide it."""
+    t = G.CLAIMED[name]
+    raw = O.quantize(t, np.random.default_rng(5800).normal(0.0, 0.02, size=(N, K)).astype(np.float32))
+    x = normal_x(K, seed=5801)
+    x[K // 2 + 3] = bad
+    y = gemv_gpu(cuda, G, t, raw, N, K, x)
+    ref = O.gemv(t, raw, N, K, x)
+    assert not np.isfinite(ref).any()
+    assert not np.isfinite(y).any(), np.flatnonzero(np.isfinite(y))[:8]

@@ -331,7 +331,7 @@ struct Backend {
     uint64_t graph_gen = 0, scratch_gen = 0;
 };
 
-// A scratch slot of at least xprep_bytes(N, K); growing it drains the stream first.
+// A scratch slot of at least gemv_scratch_bytes(N, K); growing it drains the stream first.
 void* backend_xscratch(Backend* be, int64_t N, int64_t K);
 
 // Both x-scratch slots hold at least `need` bytes (growing them waits for
@@ -356,7 +356,7 @@ bool backend_xscratch_reserve(Backend* be, size_t need) {
 }
 
 void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
-    if (!backend_xscratch_reserve(be, xprep_bytes(N, K))) return nullptr;
+    if (!backend_xscratch_reserve(be, gemv_scratch_bytes(N, K))) return nullptr;
     void* p = be->xscratch[be->xscratch_next];
     be->xscratch_next ^= 1;
     return p;
@@ -1292,7 +1292,7 @@ static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
             r.planned = r.planned && r.fused && nsharded == nseg && be->xg.ok &&
                         static_cast<size_t>(full) <= be->xg.cap_floats;
         r.rows = rows;
-        if (r.planned) need = std::max(need, xprep_bytes(rows, r.f[0].K));
+        if (r.planned) need = std::max(need, gemv_scratch_bytes(rows, r.f[0].K));
         runs.push_back(r);
         i += r.count;
     }
@@ -1751,6 +1751,7 @@ int b200_gemv_noalloc(int type, const void* w_packed, const float* x, float* y, 
         const cudaError_t e = static_scratch(&s);
         if (e != cudaSuccess) return launch_rc(e, "b200_gemv_noalloc: cudaGetSymbolAddress");
         lo.scratch = s;
+        lo.classic = true;  // the fixed area is sized for the classic kernel's scratch
     }
     return launch_rc(gemv_launch(type, w_packed, x, y, n, k, static_cast<cudaStream_t>(stream), lo),
                      "b200_gemv_noalloc");

@@ -757,7 +757,7 @@ cudaError_t gemv_launch(int type, const void* W, const float* x, float* y, int64
     if (layout_kind(type, N, K) == 1) {
         void* scratch = opts.scratch ? opts.scratch : launcher_scratch(stream, N, K);
         if (!scratch) return cudaErrorMemoryAllocation;
-        return gemv_mma_launch(type, W, x, y, N, K, scratch, stream, opts.pdl, opts.feed, opts.x_ready);
+        return gemv_mma_launch(type, W, x, y, N, K, scratch, stream, opts.pdl, opts.feed, opts.x_ready, opts.classic);
     }
     const uint8_t* w = static_cast<const uint8_t*>(W);
     switch (type) {

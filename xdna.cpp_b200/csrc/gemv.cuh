@@ -24,7 +24,9 @@ struct MmaFeed {
 
 struct LaunchOpts {
     bool pdl = false;          // programmatic dependent launch (overlap with the previous kernel)
-    void* scratch = nullptr;   // MMA-path scratch of xprep_bytes(N, K), zeroed when new (nullptr: internal)
+    void* scratch = nullptr;   // MMA-path scratch of gemv_scratch_bytes(N, K) (xprep_bytes(N, K) when
+                               // `classic`), zeroed when new (nullptr: internal)
+    bool classic = false;      // MMA path: the classic kernel only (its scratch is xprep_bytes(N, K))
     const MmaFeed* feed = nullptr;  // MMA path: this launch prepares the next launch's x
     bool x_ready = false;           // MMA path: the previous launch prepared this launch's x
 };
@@ -37,13 +39,20 @@ struct ScratchLayout {
 };
 ScratchLayout scratch_layout(int64_t N, int64_t K);
 size_t xprep_bytes(int64_t N, int64_t K);
+// Scratch of any MMA GEMV launch over N rows: xprep_bytes plus the bulk
+// kernel's split-tile chunk sums.
+size_t gemv_scratch_bytes(int64_t N, int64_t K);
+// Reads and clears the current device's GEMV error word (nonzero: a bounded
+// wait inside a bulk-copy GEMV ran out).
+cudaError_t gemv_error_status(int* out);
 void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K);
 // The fixed static-array scratch of b200_gemv_noalloc: its size, and its
 // device address on the current device (cudaGetSymbolAddress, once per device).
 size_t static_scratch_bytes();
 cudaError_t static_scratch(void** out);
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K, void* scratch,
-                            cudaStream_t stream, bool pdl, const MmaFeed* feed = nullptr, bool x_ready = false);
+                            cudaStream_t stream, bool pdl, const MmaFeed* feed = nullptr, bool x_ready = false,
+                            bool classic = false);
 // Several MMA-layout matrices of one type that multiply the same x (same K)
 // in one launch: y_s = W_s x for s < nseg <= MMA_MAX_SEGMENTS, scratch of
 // xprep_bytes(sum of N_s, K).
@@ -71,7 +80,7 @@ struct PeerExchange {
 };
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr,
-                                  const MmaFeed* feed = nullptr, bool x_ready = false);
+                                  const MmaFeed* feed = nullptr, bool x_ready = false, bool classic = false);
 // Copy the peers' rows of each segment from this GPU's exchange buffer
 // (xdata: half 0) into the full outputs once every peer's flag reaches the
 // launch's epoch, read from *epoch after the GEMV has stored it (a bounded

@@ -32,6 +32,9 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <type_traits>
 #include <mutex>
 
 #include "formats.cuh"
@@ -42,6 +45,11 @@ namespace xb {
 namespace {
 
 
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -133,7 +141,12 @@ template <int BL>
 __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t* __restrict__ frags,
                                          float* __restrict__ scale, float* __restrict__ xsum) {
     const int64_t b = (w32 * 32 + lane) / BL;  // this lane's block
-    float m = fabsf(v), s = v;
+    // a block holding an infinity or a NaN gets a NaN scale and sum, so every
+    // output it reaches is NaN, as in an F32 dot product (the fixed-point
+    // digits cannot carry it)
+    const uint32_t nonfinite = __ballot_sync(0xffffffffu, !isfinite(v));
+    const bool bad = BL == 32 ? nonfinite != 0u : ((nonfinite >> (lane & 16)) & 0xFFFFu) != 0u;
+    float m = isfinite(v) ? fabsf(v) : 0.f, s = v;
 #pragma unroll
     for (int o = BL / 2; o > 0; o >>= 1) {
         m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -143,7 +156,7 @@ __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t
     if (m > 0.f) frexpf(m, &E);  // m < 2^E
     int e = m > 0.f ? E - 22 : 0;
     e = e < -120 ? -120 : (e > 120 ? 120 : e);
-    const int X = __float2int_rn(v * ldexpf(1.0f, -e));  // |X| <= 2^22
+    const int X = isfinite(v) ? __float2int_rn(v * ldexpf(1.0f, -e)) : 0;  // |X| <= 2^22
     const int d0 = ((X + 128) & 255) - 128;
     const int X1 = (X - d0) >> 8;
     const int d1 = ((X1 + 128) & 255) - 128;
@@ -172,8 +185,8 @@ __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t
         }
     }
     if (lane % BL == 0) {
-        scale[b] = ldexpf(1.0f, e);
-        xsum[b] = s;
+        scale[b] = bad ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
+        xsum[b] = bad ? __int_as_float(0x7fc00000) : s;
     }
 }
 
@@ -344,22 +357,45 @@ struct Split {
     }
 };
 
+// Loads of a group's weights (W) and of the x fragments (X): from global
+// memory (streaming loads for the weights, the read-only cache for the
+// rest), or from a shared-memory stage filled by bulk copies.
+struct LdGlobal {
+    static __device__ __forceinline__ uint4 q(const uint8_t* p) { return ld_stream(p); }
+    static __device__ __forceinline__ uint4 q_ro(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+    static __device__ __forceinline__ uint2 d(const uint8_t* p) { return __ldg(reinterpret_cast<const uint2*>(p)); }
+    static __device__ __forceinline__ uint32_t w(const uint8_t* p) {
+        return __ldg(reinterpret_cast<const unsigned int*>(p));
+    }
+    static __device__ __forceinline__ uint32_t h(const uint8_t* p) {
+        return __ldg(reinterpret_cast<const unsigned short*>(p));
+    }
+};
+struct LdShared {
+    static __device__ __forceinline__ uint4 q(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+    static __device__ __forceinline__ uint4 q_ro(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+    static __device__ __forceinline__ uint2 d(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+    static __device__ __forceinline__ uint32_t w(const uint8_t* p) { return *reinterpret_cast<const unsigned int*>(p); }
+    static __device__ __forceinline__ uint32_t h(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
+};
+
 // One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
 // fb: this lane's B slot of chunk 0 (or the zero slot), fc: bytes between chunks.
 // Q6_K: two sets of 8 sixteen-value blocks; q = 6 bits (A = q, u8), value =
 // d * sc * (q - 32) with int8 sc per 16 values, so each block adds
 // d * sc * (2^e * T - 32 * xsum).
+template <class W, class X>
 __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* fb, int fc,
                                               const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
                                               int g, int t, float& y0, float& y8) {
     uint4 A[4], H[2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
-    H[0] = ld_stream(gb + 2048 + lane * 32);
-    H[1] = ld_stream(gb + 2048 + lane * 32 + 16);
-    const uint2 scw = __ldg(reinterpret_cast<const uint2*>(gb + 3072) + lane);
-    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 3328) + g));
-    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 3328) + g + 8));
+    for (int i = 0; i < 4; ++i) A[i] = W::q(gb + (i * 32 + lane) * 16);
+    H[0] = W::q(gb + 2048 + lane * 32);
+    H[1] = W::q(gb + 2048 + lane * 32 + 16);
+    const uint2 scw = W::d(gb + 3072 + 8 * lane);
+    const float dg = h2f(W::h(gb + 3328 + 2 * g));
+    const float d8 = h2f(W::h(gb + 3328 + 2 * (g + 8)));
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
         int C[3][4];
@@ -370,8 +406,8 @@ __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* 
 #pragma unroll
         for (int cs = 0; cs < 4; ++cs) {
             const int c = 4 * st + cs;
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-            const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+            const uint4 q = X::q_ro(fb + c * fc);
+            const uint2 r = X::d(fb + c * fc + 16);
             const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
             const uint32_t hw = word(H[c >> 2], c & 3);  // bits 8j + 2k: high pair of register k
             const uint32_t a0 = (w0 & 0x0F0F0F0Fu) | ((hw << 4) & 0x30303030u);
@@ -402,15 +438,16 @@ __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* 
 
 // Q3_K: two sets of 8 sixteen-value blocks; q3 = low pair + 4 * high bit
 // (A = q3, u8), value = d * (sc - 32) * (q3 - 4) with 6-bit sc per 16 values.
+template <class W, class X>
 __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* fb, int fc,
                                               const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
                                               int g, int t, float& y0, float& y8) {
-    const uint4 L0 = ld_stream(gb + lane * 32), L1 = ld_stream(gb + lane * 32 + 16);
-    const uint4 H = ld_stream(gb + 1024 + lane * 16);
-    const uint32_t slo = __ldg(reinterpret_cast<const unsigned int*>(gb + 1536) + lane);
-    const uint32_t shi = __ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + lane);
-    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1728) + g));
-    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1728) + g + 8));
+    const uint4 L0 = W::q(gb + lane * 32), L1 = W::q(gb + lane * 32 + 16);
+    const uint4 H = W::q(gb + 1024 + lane * 16);
+    const uint32_t slo = W::w(gb + 1536 + 4 * lane);
+    const uint32_t shi = W::h(gb + 1664 + 2 * lane);
+    const float dg = h2f(W::h(gb + 1728 + 2 * g));
+    const float d8 = h2f(W::h(gb + 1728 + 2 * (g + 8)));
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
         int C[3][4];
@@ -421,8 +458,8 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
 #pragma unroll
         for (int cs = 0; cs < 4; ++cs) {
             const int c = 4 * st + cs;
-            const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-            const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+            const uint4 q = X::q_ro(fb + c * fc);
+            const uint2 r = X::d(fb + c * fc + 16);
             const uint32_t lw = word(c < 4 ? L0 : L1, c & 3);  // bits 8j + 2k: low pair of register k
             const uint32_t hw = word(H, c >> 1);                // bit 8j + 4 (c & 1) + k: high bit
             uint32_t hk[4];
@@ -483,14 +520,15 @@ __device__ __forceinline__ void iq4nl_lookup2(uint32_t w, uint32_t& lo, uint32_t
     hi = prmt(XB_IQ4NL_XA_0, XB_IQ4NL_XA_1, w >> 16) ^ prmt(XB_IQ4NL_XB_0, XB_IQ4NL_XB_1, x >> 16);
 }
 
+template <class W, class X>
 __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t* fb, int fc,
                                                 const float* __restrict__ sc_, int lane, int g, int t, float& y0,
                                                 float& y8) {
     uint4 A[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
-    const uint2 h0 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + g);  // {d | scales_h << 16, scales_l}
-    const uint2 h8 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + g + 8);
+    for (int i = 0; i < 4; ++i) A[i] = W::q(gb + (i * 32 + lane) * 16);
+    const uint2 h0 = W::d(gb + 2048 + 8 * g);  // {d | scales_h << 16, scales_l}
+    const uint2 h8 = W::d(gb + 2048 + 8 * (g + 8));
     int C[3][4];
 #pragma unroll
     for (int p = 0; p < 3; ++p)
@@ -498,8 +536,8 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint4 q = X::q_ro(fb + c * fc);
+        const uint2 r = X::d(fb + c * fc + 16);
         uint32_t a0, a1, a2, a3;
         iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1)), a0, a1);
         iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1) + 1), a2, a3);
@@ -549,16 +587,17 @@ __device__ __forceinline__ uint32_t iq3s_reg(uint32_t iw, uint32_t hw, uint32_t 
     return signed4(s_iq3s_grid[idx], (sw >> (4 * k)) & 0xFu);
 }
 
+template <class W, class X>
 __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t* fb, int fc,
                                                const float* __restrict__ sc_, int lane, int g, int t, float& y0,
                                                float& y8) {
-    const uint4 I0 = ld_stream(gb + lane * 32), I1 = ld_stream(gb + lane * 32 + 16);
-    const uint4 S = ld_stream(gb + 1024 + lane * 16);
-    const uint32_t qh = __ldg(reinterpret_cast<const unsigned int*>(gb + 1536) + lane);
-    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + g));
-    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1664) + g + 8));
-    const uint32_t sg = __ldg(reinterpret_cast<const unsigned int*>(gb + 1696) + g);
-    const uint32_t s8 = __ldg(reinterpret_cast<const unsigned int*>(gb + 1696) + g + 8);
+    const uint4 I0 = W::q(gb + lane * 32), I1 = W::q(gb + lane * 32 + 16);
+    const uint4 S = W::q(gb + 1024 + lane * 16);
+    const uint32_t qh = W::w(gb + 1536 + 4 * lane);
+    const float dg = h2f(W::h(gb + 1664 + 2 * g));
+    const float d8 = h2f(W::h(gb + 1664 + 2 * (g + 8)));
+    const uint32_t sg = W::w(gb + 1696 + 4 * g);
+    const uint32_t s8 = W::w(gb + 1696 + 4 * (g + 8));
     int C[3][4];
 #pragma unroll
     for (int p = 0; p < 3; ++p)
@@ -566,8 +605,8 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint4 q = X::q_ro(fb + c * fc);
+        const uint2 r = X::d(fb + c * fc + 16);
         const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
         const uint32_t sw = word(S, c >> 1) >> (16 * (c & 1));
         const uint32_t hw = qh >> (4 * c);
@@ -597,13 +636,14 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
 // are a 7-bit index plus the bit that makes the count of negatives even.
 __shared__ uint32_t s_iq3xxs_grid[256];
 
+template <class W, class X>
 __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_t* fb, int fc,
                                                  const float* __restrict__ sc_, int lane, int g, int t, float& y0,
                                                  float& y8) {
-    const uint4 I0 = ld_stream(gb + lane * 32), I1 = ld_stream(gb + lane * 32 + 16);
-    const uint4 SS = ld_stream(gb + 1024 + lane * 16);
-    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1536) + g));
-    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1536) + g + 8));
+    const uint4 I0 = W::q(gb + lane * 32), I1 = W::q(gb + lane * 32 + 16);
+    const uint4 SS = W::q(gb + 1024 + lane * 16);
+    const float dg = h2f(W::h(gb + 1536 + 2 * g));
+    const float d8 = h2f(W::h(gb + 1536 + 2 * (g + 8)));
     int C[3][4];
 #pragma unroll
     for (int p = 0; p < 3; ++p)
@@ -611,8 +651,8 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint4 q = X::q_ro(fb + c * fc);
+        const uint2 r = X::d(fb + c * fc + 16);
         const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
         const uint32_t w = word(SS, c >> 1);
         uint32_t a[4];
@@ -647,15 +687,16 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
 // chunks 2q and 2q + 1 of one register: one 64-bit load feeds two registers.
 __shared__ unsigned long long s_iq2s_grid[1024];
 
+template <class W, class X>
 __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t* fb, int fc,
                                                const float* __restrict__ sc_, int lane, int g, int t, float& y0,
                                                float& y8) {
-    const uint4 IL = ld_stream(gb + lane * 16);
-    const uint4 SG = ld_stream(gb + 512 + lane * 16);
-    const uint32_t qh = __ldg(reinterpret_cast<const unsigned int*>(gb + 1024) + lane);
-    const uint32_t scw = __ldg(reinterpret_cast<const unsigned int*>(gb + 1152) + lane);
-    const float dg = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1280) + g));
-    const float d8 = h2f(__ldg(reinterpret_cast<const unsigned short*>(gb + 1280) + g + 8));
+    const uint4 IL = W::q(gb + lane * 16);
+    const uint4 SG = W::q(gb + 512 + lane * 16);
+    const uint32_t qh = W::w(gb + 1024 + 4 * lane);
+    const uint32_t scw = W::w(gb + 1152 + 4 * lane);
+    const float dg = h2f(W::h(gb + 1280 + 2 * g));
+    const float d8 = h2f(W::h(gb + 1280 + 2 * (g + 8)));
 #pragma unroll
     for (int st = 0; st < 2; ++st) {
         int C[3][4];
@@ -679,8 +720,8 @@ __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t*
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int c = 4 * st + 2 * qq + h;
-                const uint4 bq = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-                const uint2 br = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+                const uint4 bq = X::q_ro(fb + c * fc);
+                const uint2 br = X::d(fb + c * fc + 16);
                 const uint32_t* a = h ? hi : lo;
                 mma_s8s8(C[0], a[0], a[1], a[2], a[3], bq.x, bq.y);
                 mma_s8s8(C[1], a[0], a[1], a[2], a[3], bq.z, bq.w);
@@ -705,21 +746,21 @@ __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t*
 }
 
 // Q4_0, Q4_K, Q5_K: one set of 8 thirty-two-value blocks, 4- or 5-bit q.
-template <int TYPE>
+template <int TYPE, class W, class X>
 __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* fb, int fc,
                                               const float* __restrict__ sc_, const float* __restrict__ xs_, int lane,
                                               int g, int t, float& y0, float& y8) {
     uint4 A[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) A[i] = ld_stream(gb + (i * 32 + lane) * 16);
+    for (int i = 0; i < 4; ++i) A[i] = W::q(gb + (i * 32 + lane) * 16);
     uint4 h0, h8, H;
     uint2 d4;
-    if (TYPE == T_Q5_K) H = ld_stream(gb + 2048 + lane * 16);  // fifth bits
+    if (TYPE == T_Q5_K) H = W::q(gb + 2048 + lane * 16);  // fifth bits
     if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        h0 = ld_stream(gb + kHeaderOff<TYPE> + 16 * g);
-        h8 = ld_stream(gb + kHeaderOff<TYPE> + 16 * (g + 8));
+        h0 = W::q(gb + kHeaderOff<TYPE> + 16 * g);
+        h8 = W::q(gb + kHeaderOff<TYPE> + 16 * (g + 8));
     } else {
-        d4 = __ldg(reinterpret_cast<const uint2*>(gb + 2048) + lane);
+        d4 = W::d(gb + 2048 + 8 * lane);
     }
     int C[3][4];
 #pragma unroll
@@ -728,8 +769,8 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(fb + c * fc));
-        const uint2 r = __ldg(reinterpret_cast<const uint2*>(fb + c * fc + 16));
+        const uint4 q = X::q_ro(fb + c * fc);
+        const uint2 r = X::d(fb + c * fc + 16);
         const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
         uint32_t a0, a1, a2, a3;
         if (TYPE == T_Q5_K) {
@@ -802,24 +843,24 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
     }
 }
 
-template <int TYPE>
+template <int TYPE, class W = LdGlobal, class X = LdGlobal>
 __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, int fc, const float* __restrict__ sc_,
                                           const float* __restrict__ xs_, int lane, int g, int t, float& y0,
                                           float& y8) {
     if constexpr (TYPE == T_Q6_K)
-        group_dot_q6k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+        group_dot_q6k<W, X>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_Q3_K)
-        group_dot_q3k(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+        group_dot_q3k<W, X>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ4_XS)
-        group_dot_iq4xs(gb, fb, fc, sc_, lane, g, t, y0, y8);
+        group_dot_iq4xs<W, X>(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ3_S)
-        group_dot_iq3s(gb, fb, fc, sc_, lane, g, t, y0, y8);
+        group_dot_iq3s<W, X>(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ3_XXS)
-        group_dot_iq3xxs(gb, fb, fc, sc_, lane, g, t, y0, y8);
+        group_dot_iq3xxs<W, X>(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else if constexpr (TYPE == T_IQ2_S)
-        group_dot_iq2s(gb, fb, fc, sc_, lane, g, t, y0, y8);
+        group_dot_iq2s<W, X>(gb, fb, fc, sc_, lane, g, t, y0, y8);
     else
-        group_dot_nib<TYPE>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
+        group_dot_nib<TYPE, W, X>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
 
 // After a warp has written all 16 rows of `tile`: if the tile feeds the next
@@ -1015,6 +1056,374 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     }
 }
 
+// ---------------------------------------------------------------------------
+// Bulk-copy GEMV: the weights reach shared memory through the TMA unit
+// (cp.async.bulk into an mbarrier-tracked ring) and the work is handed out
+// in chunks, so the SMs that stream fastest take more of it.
+//
+// One CTA per SM: kCons consumer warps and one producer warp (one thread of
+// it issues the copies).  A chunk is kCons consecutive units of one tile (the
+// last chunk of a tile may be shorter), or, when a tile has fewer groups and
+// kCons is a multiple of that count, kCons / ngroups whole tiles; consumer
+// warp w computes unit w of every chunk.  Each stage of the ring holds one
+// chunk's weights (and, in the staged-x variant, its x fragments).
+//   * Producer: the first `stages` chunks of CTA c are fixed (c, c + grid,
+//     ...) and their weights are requested before the programmatic-launch
+//     wait, while the previous kernel still runs; after the wait, chunks come
+//     from a ticket counter (cleared with the launch's other counters).  A
+//     stage is refilled when all consumer warps have arrived on its `empty`
+//     barrier; a chunk index of -1 in a stage ends the consumers' loop.
+//   * Consumers: wait for the stage's `full` barrier, compute their unit,
+//     release the stage, and write their 16 partial rows to shared memory;
+//     after a named barrier one warp adds the chunk's partial rows in warp
+//     order.  A tile whose groups span several chunks has its chunk sums
+//     written to global memory (slot = tile, chunk of the tile); the last
+//     chunk to count in at the tile's counter adds them in chunk order.  The
+//     order of every addition is fixed by the shape alone, so results are
+//     deterministic.
+// Every wait is bounded (2 s of %globaltimer); a wait that runs out sets the
+// launch's error word and ends the CTA's loop instead of hanging.
+// ---------------------------------------------------------------------------
+constexpr int kCons = 16;
+constexpr int kBulkThreads = (kCons + 1) * 32;
+constexpr uint64_t kBulkWaitNs = 2000000000ull;
+
+struct BulkArgs {
+    int nchunks;      // chunks of the launch
+    int nck;          // chunks per tile (split mode), 0 in whole-tile mode
+    int tpc;          // tiles per chunk (whole-tile mode)
+    int ntiles;
+    int stages;       // ring depth
+    int stage_bytes;  // one stage: kCons units of weights (+ their x fragments when staged)
+    float* cpart;     // chunk sums of split tiles: [tile][chunk of the tile][16 rows]
+    int* ticket;      // next dynamic chunk
+    int* err;         // set when a bounded wait runs out
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for the completion of the barrier phase with parity `parity`.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t now = global_ns();
+            if (i == 0) t0 = now;
+            else if (*abort || now - t0 > kBulkWaitNs) return false;
+        }
+    }
+}
+// Global -> shared bulk copy completing on `bar` (16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Shared-memory layout of the bulk kernel after the ring (the host sizes it
+// with the same arithmetic): the barriers full[S], empty[S], ready[2],
+// freed[2] and fin, the stages' chunk indices, two sets of per-warp partial
+// rows, a zero slot and the abort flag.
+__host__ __device__ constexpr size_t bulk_bars_off(int S, int stage_bytes) { return size_t(S) * stage_bytes; }
+__host__ __device__ constexpr size_t bulk_part_off(int S, int stage_bytes) {
+    return (bulk_bars_off(S, stage_bytes) + 8 * (2 * size_t(S) + 5) + 4 * size_t(S) + 15) & ~size_t(15);
+}
+__host__ __device__ constexpr size_t bulk_smem_bytes(int S, int stage_bytes) {
+    return bulk_part_off(S, stage_bytes) + 2 * kCons * MMA_TILE_ROWS * sizeof(float) + kSlotBytes + 16;
+}
+
+template <int TYPE, bool kXS>
+__global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvArgs a, const BulkArgs b) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int UB = kUnitBytes<TYPE>;
+    const int S = b.stages, SB = b.stage_bytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + bulk_bars_off(S, SB));
+    uint64_t* empty = full + S;
+    uint64_t* ready = empty + S;  // [2]: the consumers' partial rows of a chunk are written
+    uint64_t* freed = ready + 2;  // [2]: the reducer has read them
+    uint64_t* fin = freed + 2;    // every consumer warp has left its loop
+    int* s_chunk = reinterpret_cast<int*>(fin + 1);
+    float* s_part = reinterpret_cast<float*>(smem + bulk_part_off(S, SB));
+    uint32_t* s_zero = reinterpret_cast<uint32_t*>(s_part + 2 * kCons * MMA_TILE_ROWS);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_zero + kSlotBytes / 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int ng = static_cast<int>(a.ngroups);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kCons);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(ready + i, kCons);
+            mbar_init(freed + i, 1);
+        }
+        mbar_init(fin, kCons);
+        *s_abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (threadIdx.x < kSlotBytes / 4) s_zero[threadIdx.x] = 0u;
+    if constexpr (TYPE == T_IQ3_S)
+        for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
+    if constexpr (TYPE == T_IQ3_XXS)
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_iq3xxs_grid[i] = kIq3xxsGrid[i];
+    if constexpr (TYPE == T_IQ2_S)
+        for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s_grid[i] = kIq2sGrid[i];
+    __syncthreads();
+    pdl_release();
+
+    if (warp == kCons) {
+        // ------------------------------------------------------- producer
+        if (lane != 0) return;
+        auto weights = [&](int c, int stage, bool arrive) -> uint32_t {
+            uint8_t* dst = smem + size_t(stage) * SB;
+            uint32_t bytes = 0;
+            s_chunk[stage] = c;
+            if (b.nck > 0) {
+                const int tile = c / b.nck, g0 = (c - tile * b.nck) * kCons;
+                const int gc = ng - g0 < kCons ? ng - g0 : kCons;
+                const SegRef sr = seg_ref(a, tile);
+                bytes = static_cast<uint32_t>(gc * UB);
+                if (arrive) mbar_arrive_tx(full + stage, bytes + (kXS ? gc * kGroupFragBytes : 0));
+                else mbar_expect_tx(full + stage, bytes);
+                bulk_g2s(dst, sr.W + ((int64_t(tile) - sr.first_tile) * ng + g0) * UB, bytes, full + stage);
+            } else {
+                const int t0 = c * b.tpc, nt = b.ntiles - t0 < b.tpc ? b.ntiles - t0 : b.tpc;
+                bytes = static_cast<uint32_t>(nt * ng * UB);
+                if (arrive) mbar_arrive_tx(full + stage, bytes + (kXS ? ng * kGroupFragBytes : 0));
+                else mbar_expect_tx(full + stage, bytes);
+                for (int j = 0; j < nt; ++j) {
+                    const SegRef sr = seg_ref(a, t0 + j);
+                    bulk_g2s(dst + j * ng * UB, sr.W + (int64_t(t0 + j) - sr.first_tile) * ng * UB,
+                             static_cast<uint32_t>(ng * UB), full + stage);
+                }
+            }
+            return bytes;
+        };
+        // x fragments of chunk c (staged-x variant): written by the previous
+        // launch or the x preparation, so only after the dependency wait
+        auto xfrags = [&](int c, int stage, bool arrive) {
+            const int g0 = b.nck > 0 ? (c % b.nck) * kCons : 0;
+            const int gc = b.nck > 0 ? (ng - g0 < kCons ? ng - g0 : kCons) : ng;
+            const uint32_t bytes = static_cast<uint32_t>(gc * kGroupFragBytes);
+            if (arrive) mbar_arrive_tx(full + stage, bytes);
+            bulk_g2s(smem + size_t(stage) * SB + kCons * UB, a.frags + int64_t(g0) * kGroupFragBytes, bytes,
+                     full + stage);
+        };
+        const int grid = static_cast<int>(gridDim.x);
+        int it = 0;
+        for (; it < S; ++it) {  // the fixed chunks: weights only, before the dependency wait
+            const int c = static_cast<int>(blockIdx.x) + it * grid;
+            if (c >= b.nchunks) break;
+            weights(c, it, !kXS);
+        }
+        const int fixed = it;
+        pdl_wait();
+        if (kXS)
+            for (int i = 0; i < fixed; ++i) xfrags(static_cast<int>(blockIdx.x) + i * grid, i, true);
+        bool more = fixed == S;
+        while (more) {
+            const int c = S * grid + atomicAdd(b.ticket, 1);
+            const int stage = it % S;
+            if (!mbar_wait(empty + stage, static_cast<uint32_t>((it / S) - 1) & 1u, s_abort)) {
+                atomicExch(b.err, 1);
+                *s_abort = 1;
+                return;
+            }
+            if (c >= b.nchunks) break;
+            weights(c, stage, true);
+            if (kXS) xfrags(c, stage, false);
+            ++it;
+        }
+        // end of the work: a stage whose chunk index is -1 (its previous use,
+        // if any, was released above)
+        const int stage = it % S;
+        s_chunk[stage] = -1;
+        mbar_arrive(full + stage);
+        return;
+    }
+
+    // ----------------------------------------------------------- consumers
+    pdl_wait();  // x fragments, scales, sums and cleared counters are ready
+    uint32_t xe = 0;
+    int64_t hoff = 0;
+    if (a.xchg) {
+        xe = __ldcg(a.x.epoch) + 1u;
+        hoff = (xe & 1u) ? a.x.half_floats : 0;
+    }
+    const int ctid = warp * 32 + lane;
+    if (a.f_bl != 0) {
+        const int64_t gt = int64_t(blockIdx.x) * (kCons * 32) + ctid;
+        for (int64_t i = gt; i < a.f_ncount; i += int64_t(gridDim.x) * (kCons * 32)) a.f_count[i] = 0;
+        if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
+    }
+    const bool supplier = g == t || g == t + 4;
+    const int fc = supplier ? kChunkFragBytes : 0;
+    bool ok = true;
+    for (int it = 0;; ++it) {
+        const int stage = it % S, par = it & 1;
+        if (!mbar_wait(full + stage, static_cast<uint32_t>(it / S) & 1u, s_abort)) {
+            ok = false;
+            break;
+        }
+        const int c = s_chunk[stage];
+        if (c < 0) break;
+        int tile, gi, gc, k = 0;
+        if (b.nck > 0) {
+            tile = c / b.nck;
+            k = c - tile * b.nck;
+            gi = k * kCons + warp;
+            gc = ng - k * kCons < kCons ? ng - k * kCons : kCons;
+        } else {
+            tile = c * b.tpc + warp / ng;
+            gi = warp % ng;
+            gc = (b.ntiles - c * b.tpc < b.tpc ? b.ntiles - c * b.tpc : b.tpc) * ng;
+        }
+        float y0 = 0.f, y8 = 0.f;
+        if (warp < gc) {
+            const uint8_t* st = smem + size_t(stage) * SB;
+            const uint8_t* fb;
+            if constexpr (kXS)
+                fb = supplier ? st + kCons * UB + (b.nck > 0 ? warp : gi) * kGroupFragBytes + g * kSlotBytes
+                              : reinterpret_cast<const uint8_t*>(s_zero);
+            else
+                fb = supplier ? a.frags + int64_t(gi) * kGroupFragBytes + g * kSlotBytes : a.zeros;
+            group_dot<TYPE, LdShared, typename std::conditional<kXS, LdShared, LdGlobal>::type>(
+                st + warp * UB, fb, fc, a.scale + int64_t(gi) * kXBlocks<TYPE>, a.xsum + int64_t(gi) * kXBlocks<TYPE>,
+                lane, g, t, y0, y8);
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+            y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+            y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + stage);  // this warp is done with the stage
+        // partial rows of this chunk: the buffer of this parity was last read
+        // by the reducer two chunks ago
+        if (it >= 2 && !mbar_wait(freed + par, static_cast<uint32_t>((it >> 1) - 1) & 1u, s_abort)) {
+            ok = false;
+            break;
+        }
+        float* part = s_part + par * kCons * MMA_TILE_ROWS;
+        if (t == 0) {
+            part[warp * MMA_TILE_ROWS + g] = y0;
+            part[warp * MMA_TILE_ROWS + g + 8] = y8;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ready + par);
+        if (warp != c % kCons) continue;
+        // this warp reduces the chunk: add the warps' partial rows in warp order
+        if (!mbar_wait(ready + par, static_cast<uint32_t>(it >> 1) & 1u, s_abort)) {
+            ok = false;
+            break;
+        }
+        const int r = lane & 15;
+        if (b.nck > 0) {
+            float acc = 0.f;
+            for (int v = 0; v < gc; ++v) acc += part[v * MMA_TILE_ROWS + r];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(freed + par);
+            const SegRef sr = seg_ref(a, tile);
+            float* ty = sr.y + (int64_t(tile) - sr.first_tile) * MMA_TILE_ROWS;
+            bool emitted = false;
+            if (b.nck == 1) {
+                if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc, hoff);
+                emitted = true;
+            } else {
+                float* slots = b.cpart + int64_t(tile) * b.nck * MMA_TILE_ROWS;
+                if (lane < MMA_TILE_ROWS) slots[k * MMA_TILE_ROWS + r] = acc;
+                __threadfence();
+                __syncwarp();
+                int prev = 0;
+                if (lane == 0) prev = atomicAdd(a.count + tile, 1);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                if (prev == b.nck - 1) {  // the tile's last chunk: add the chunk sums in chunk order
+                    __threadfence();
+                    float sum = 0.f;
+                    if (lane < MMA_TILE_ROWS)
+                        for (int kk = 0; kk < b.nck; ++kk) sum += __ldcg(slots + kk * MMA_TILE_ROWS + r);
+                    if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, sum, hoff);
+                    emitted = true;
+                }
+            }
+            if (emitted && a.f_bl != 0 && tile >= a.f_t0 && tile < a.f_t1)
+                feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl,
+                          lane);
+        } else {
+            // whole tiles: tile j of the chunk is warps j ng .. j ng + ng - 1
+            const int ntc = gc / ng;
+            float acc[kCons];
+#pragma unroll
+            for (int j = 0; j < kCons; ++j) {
+                acc[j] = 0.f;
+                if (j < ntc)
+                    for (int v = 0; v < ng; ++v) acc[j] += part[(j * ng + v) * MMA_TILE_ROWS + r];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(freed + par);
+#pragma unroll
+            for (int j = 0; j < kCons; ++j) {
+                if (j >= ntc) break;
+                const int tj = c * b.tpc + j;
+                const SegRef sr = seg_ref(a, tj);
+                float* ty = sr.y + (int64_t(tj) - sr.first_tile) * MMA_TILE_ROWS;
+                if (lane < MMA_TILE_ROWS) emit(a, ty, tj, r, acc[j], hoff);
+                if (a.f_bl != 0 && tj >= a.f_t0 && tj < a.f_t1)
+                    feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tj - a.f_t0), a.f_bl,
+                              lane);
+            }
+        }
+    }
+    if (!ok) {
+        if (lane == 0) atomicExch(b.err, 1);
+        *s_abort = 1;
+        return;
+    }
+    if (a.xchg) {
+        // as in gemv_mma_kernel: every row this CTA stored is ordered before
+        // its count-in; the last CTA fences at system scope once and raises
+        // the peers' flags
+        __syncwarp();
+        if (lane == 0) mbar_arrive(fin);
+        if (ctid == 0) {
+            if (!mbar_wait(fin, 0u, s_abort)) {
+                atomicExch(b.err, 1);
+                return;
+            }
+            __threadfence();
+            if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
+                __threadfence_system();
+                for (int p = 0; p < a.x.world; ++p)
+                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, xe);
+                *a.x.epoch = xe;
+            }
+        }
+    }
+}
+
 // Peers' rows -> the full outputs, after every peer's flag reached `epoch`.
 // Launched with programmatic dependent launch: it first waits
 // (griddepcontrol.wait) for this GPU's GEMV to complete, which also makes the
@@ -1023,11 +1432,6 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
 // %globaltimer); on time-out *err is set and nothing is copied, so the host
 // reports an error instead of the GPU hanging.
 constexpr uint64_t kGatherWaitNs = 1000000000ull;  // 1 s of %globaltimer
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 struct GatherArgs {
     GatherSeg seg[kMaxSegs];
     int nseg;
@@ -1230,10 +1634,19 @@ static int sm_count() {
 }
 
 // Counters of a launch over `ntiles` tiles: one per tile, the CTA completion
-// counter, and one per 32-value chunk of an output that feeds the next launch.
-// All start at zero: cleared by the x-preparation kernel, or by the launch
-// before when that one prepares x.
-static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1; }
+// counter, one per 32-value chunk of an output that feeds the next launch,
+// and the bulk kernel's chunk ticket (the last one).  All start at zero:
+// cleared by the x-preparation kernel, or by the launch before when that one
+// prepares x.
+static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1 + 1; }
+
+// Chunk sums of the bulk kernel's split tiles, after the layout above:
+// [tile][chunk of the tile][16 rows] floats.
+static size_t bulk_cpart_bytes(int64_t N, int64_t K) {
+    const int64_t ng = K / 256;
+    return ng > kCons ? size_t(N / MMA_TILE_ROWS) * size_t((ng + kCons - 1) / kCons) * MMA_TILE_ROWS * sizeof(float)
+                      : 0;
+}
 
 // Scratch of one MMA GEMV launch (layout described above the kernels).
 ScratchLayout scratch_layout(int64_t N, int64_t K) {
@@ -1252,6 +1665,154 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
 }
 
 size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
+
+size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total + bulk_cpart_bytes(N, K); }
+
+// Which GEMV kernel serves MMA-layout launches: XDNA_B200_GEMV = "classic"
+// (gemv_mma_kernel), "bulk" (gemv_bulk_kernel, x fragments through the L1) or
+// "bulkx" (gemv_bulk_kernel with the x fragments staged beside the weights).
+// Read once per process.
+static int gemv_kernel_choice() {
+    static const int choice = [] {
+        const char* v = getenv("XDNA_B200_GEMV");
+        if (v && !strcmp(v, "classic")) return 0;
+        if (v && !strcmp(v, "bulkx")) return 2;
+        return 1;
+    }();
+    return choice;
+}
+
+// Error word of the bulk kernel's bounded waits on the current device.
+static __device__ int g_gemv_err;
+static int* gemv_err_ptr() {
+    static std::mutex m;
+    static int* addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(m);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemv_err) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<int*>(p);
+    }
+    return addr[dev];
+}
+
+cudaError_t gemv_error_status(int* out) {
+    int* p = gemv_err_ptr();
+    if (!p) return cudaErrorInvalidDevice;
+    int v = 0;
+    cudaError_t e = cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && v) e = cudaMemset(p, 0, sizeof(int));
+    *out = v;
+    return e;
+}
+
+// Launch plan of the bulk kernel for one launch, or false where it does not
+// apply (a tile count of groups that neither fills a chunk nor divides kCons,
+// or no room for two stages).
+struct BulkPlan {
+    BulkArgs b;
+    int grid;
+    size_t smem;
+};
+template <int TYPE>
+static bool bulk_plan(bool staged_x, int64_t ngroups, int64_t ntiles, int sms, BulkPlan* p) {
+    constexpr int UB = kUnitBytes<TYPE>;
+    // shared memory per CTA (227 KiB) less the static grid table of the IQ formats
+    constexpr size_t kGrid = TYPE == T_IQ2_S ? 8192 : (TYPE == T_IQ3_S ? 2048 : (TYPE == T_IQ3_XXS ? 1024 : 0));
+    const size_t budget = 227 * 1024 - kGrid - 1024;
+    BulkArgs& b = p->b;
+    b = BulkArgs{};
+    if (ngroups >= kCons) {
+        b.nck = static_cast<int>((ngroups + kCons - 1) / kCons);
+        b.tpc = 0;
+        if (ntiles * b.nck >= (int64_t(1) << 31)) return false;
+        b.nchunks = static_cast<int>(ntiles * b.nck);
+    } else if (ngroups > 0 && kCons % ngroups == 0) {
+        b.nck = 0;
+        b.tpc = static_cast<int>(kCons / ngroups);
+        b.nchunks = static_cast<int>((ntiles + b.tpc - 1) / b.tpc);
+    } else {
+        return false;
+    }
+    b.ntiles = static_cast<int>(ntiles);
+    b.stage_bytes = ((kCons * UB + (staged_x ? kCons * kGroupFragBytes : 0)) + 127) & ~127;
+    int S = 8;
+    while (S >= 2 && bulk_smem_bytes(S, b.stage_bytes) > budget) --S;
+    if (S < 2) return false;
+    b.stages = S;
+    p->smem = bulk_smem_bytes(S, b.stage_bytes);
+    p->grid = b.nchunks < sms ? b.nchunks : sms;
+    return true;
+}
+
+template <int TYPE, bool kXS>
+static cudaError_t launch_bulk_typed(cudaLaunchConfig_t& cg, const GemvArgs& a, const BulkArgs& b) {
+    static std::atomic<size_t> smem_set[kMaxDevices];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (smem_set[dev].load() < cg.dynamicSmemBytes) {
+        e = cudaFuncSetAttribute(gemv_bulk_kernel<TYPE, kXS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(cg.dynamicSmemBytes));
+        if (e != cudaSuccess) return e;
+        smem_set[dev].store(cg.dynamicSmemBytes);
+    }
+    return cudaLaunchKernelEx(&cg, gemv_bulk_kernel<TYPE, kXS>, a, b);
+}
+
+// Plans and launches the bulk kernel for `type`; *used = false (nothing
+// launched) where it does not apply.
+static cudaError_t launch_bulk(int type, bool staged_x, const GemvArgs& a, int64_t ntiles, int sms, uint8_t* base,
+                               const ScratchLayout& L, cudaStream_t stream, bool* used) {
+    BulkPlan p;
+    bool ok = false;
+    switch (type) {
+        case T_Q4_K: ok = bulk_plan<T_Q4_K>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_Q5_K: ok = bulk_plan<T_Q5_K>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_Q6_K: ok = bulk_plan<T_Q6_K>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_Q3_K: ok = bulk_plan<T_Q3_K>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_IQ4_XS: ok = bulk_plan<T_IQ4_XS>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_IQ3_S: ok = bulk_plan<T_IQ3_S>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_IQ3_XXS: ok = bulk_plan<T_IQ3_XXS>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        case T_IQ2_S: ok = bulk_plan<T_IQ2_S>(staged_x, a.ngroups, ntiles, sms, &p); break;
+        default: ok = bulk_plan<T_Q4_0>(staged_x, a.ngroups, ntiles, sms, &p); break;
+    }
+    *used = false;
+    if (!ok) return cudaSuccess;
+    p.b.cpart = reinterpret_cast<float*>(base + L.total);
+    p.b.ticket = a.count + counter_ints(ntiles) - 1;
+    p.b.err = gemv_err_ptr();
+    if (!p.b.err) return cudaErrorInvalidDevice;
+    cudaLaunchConfig_t cg = {};
+    cg.gridDim = dim3(static_cast<unsigned>(p.grid));
+    cg.blockDim = dim3(kBulkThreads);
+    cg.dynamicSmemBytes = p.smem;
+    cg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;  // weights are requested before the dependency wait
+    cg.attrs = attr;
+    cg.numAttrs = 1;
+    *used = true;
+#define XB_BULK(T)                                                                        \
+    case T:                                                                               \
+        return staged_x ? launch_bulk_typed<T, true>(cg, a, p.b) : launch_bulk_typed<T, false>(cg, a, p.b);
+    switch (type) {
+        XB_BULK(T_Q4_K)
+        XB_BULK(T_Q5_K)
+        XB_BULK(T_Q6_K)
+        XB_BULK(T_Q3_K)
+        XB_BULK(T_IQ4_XS)
+        XB_BULK(T_IQ3_S)
+        XB_BULK(T_IQ3_XXS)
+        XB_BULK(T_IQ2_S)
+        default: return staged_x ? launch_bulk_typed<T_Q4_0, true>(cg, a, p.b) : launch_bulk_typed<T_Q4_0, false>(cg, a, p.b);
+    }
+#undef XB_BULK
+}
 
 // One thread per (tile, group) through the shared host/device routines of
 // formats.cuh: the repack path of the 5-bit layout (a one-time upload cost).
@@ -1311,14 +1872,15 @@ static cudaError_t launch_gemv(int type, cudaLaunchConfig_t& cg, const GemvArgs&
 }
 
 cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, int64_t N, int64_t K,
-                            void* scratch, cudaStream_t stream, bool pdl, const MmaFeed* feed, bool x_ready) {
+                            void* scratch, cudaStream_t stream, bool pdl, const MmaFeed* feed, bool x_ready,
+                            bool classic) {
     const MmaSegment seg{W, y, N};
-    return gemv_mma_multi_launch(type, &seg, 1, x, K, scratch, stream, pdl, nullptr, feed, x_ready);
+    return gemv_mma_multi_launch(type, &seg, 1, x, K, scratch, stream, pdl, nullptr, feed, x_ready, classic);
 }
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg,
-                                  const MmaFeed* feed, bool x_ready) {
+                                  const MmaFeed* feed, bool x_ready, bool classic) {
     if (layout_kind(type, MMA_TILE_ROWS, 256) != 1 ||
         nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
@@ -1422,6 +1984,12 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         if (e != cudaSuccess) return e;
     }
 
+    const int choice = classic ? 0 : gemv_kernel_choice();
+    if (choice != 0) {
+        bool used = false;
+        const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, base, L, stream, &used);
+        if (used || e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks));
     cg.blockDim = dim3(kGemvThreads);
@@ -1518,7 +2086,7 @@ cudaError_t static_scratch(void** out) {
 // x preparation writing the other.  Grown on demand (must not happen inside
 // stream capture: the first call for a new, larger K allocates).
 void* launcher_scratch(cudaStream_t stream, int64_t N, int64_t K) {
-    const size_t need = xprep_bytes(N, K);
+    const size_t need = gemv_scratch_bytes(N, K);
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(g_scratch_mtx);
