@@ -1058,45 +1058,41 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
 
 // ---------------------------------------------------------------------------
 // Bulk-copy GEMV: the weights reach shared memory through the TMA unit
-// (cp.async.bulk into an mbarrier-tracked ring) and the work is handed out
-// in chunks, so the SMs that stream fastest take more of it.
+// (cp.async.bulk into an mbarrier-tracked ring), issued by one producer thread
+// ahead of kCons consumer warps.  One CTA per SM.
 //
-// One CTA per SM: kCons consumer warps and one producer warp (one thread of
-// it issues the copies).  A chunk is kCons consecutive units of one tile (the
-// last chunk of a tile may be shorter), or, when a tile has fewer groups and
-// kCons is a multiple of that count, kCons / ngroups whole tiles; consumer
-// warp w computes unit w of every chunk.  Each stage of the ring holds one
-// chunk's weights (and, in the staged-x variant, its x fragments).
-//   * Producer: the first `stages` chunks of CTA c are fixed (c, c + grid,
-//     ...) and their weights are requested before the programmatic-launch
-//     wait, while the previous kernel still runs; after the wait, chunks come
-//     from a ticket counter (cleared with the launch's other counters).  A
-//     stage is refilled when all consumer warps have arrived on its `empty`
-//     barrier; a chunk index of -1 in a stage ends the consumers' loop.
-//   * Consumers: wait for the stage's `full` barrier, compute their unit,
-//     release the stage, and write their 16 partial rows to shared memory;
-//     after a named barrier one warp adds the chunk's partial rows in warp
-//     order.  A tile whose groups span several chunks has its chunk sums
-//     written to global memory (slot = tile, chunk of the tile); the last
-//     chunk to count in at the tile's counter adds them in chunk order.  The
-//     order of every addition is fixed by the shape alone, so results are
-//     deterministic.
+// Work split.  Split mode (a tile has at least kCons groups): CTA c takes the
+// contiguous unit range [c U / G, (c + 1) U / G), walked in pieces of up to
+// kCons units that never cross a tile; consumer warp w computes unit w of
+// each piece and keeps its rows' sums in registers across the pieces of one
+// tile.  After the CTA's last piece of a tile every warp writes its 16 partial
+// rows to shared memory, and one warp adds them in warp order: a tile wholly
+// inside the CTA's range is written out; a tile shared with neighbouring CTAs
+// (only a CTA's first and last tile can be) goes through the two-slot
+// cross-CTA combine of gemv_mma_kernel, the last CTA adding the CTAs' sums in
+// CTA order.  Whole-tile mode (fewer groups, kCons a multiple of the count):
+// CTA c takes tiles [c T / G, (c + 1) T / G), kCons / ngroups tiles per
+// piece, and tile j of a piece is warps j ngroups .. (j + 1) ngroups - 1.
+// Every addition happens in an order fixed by the shape, so results are
+// deterministic.
+//
+// Overlap.  The producer requests the first `stages` pieces before the
+// programmatic-launch wait (weights are never written by the kernels this
+// one overlaps), so a launch's first bytes stream in while the previous
+// kernel drains.  In the staged-x variant each stage also carries the
+// piece's x fragments, copied after the wait.
+//
 // Every wait is bounded (2 s of %globaltimer); a wait that runs out sets the
-// launch's error word and ends the CTA's loop instead of hanging.
+// error word and ends the CTA's work instead of hanging.
 // ---------------------------------------------------------------------------
 constexpr int kCons = 16;
 constexpr int kBulkThreads = (kCons + 1) * 32;
 constexpr uint64_t kBulkWaitNs = 2000000000ull;
 
 struct BulkArgs {
-    int nchunks;      // chunks of the launch
-    int nck;          // chunks per tile (split mode), 0 in whole-tile mode
-    int tpc;          // tiles per chunk (whole-tile mode)
-    int ntiles;
+    int whole;        // whole-tile mode
     int stages;       // ring depth
     int stage_bytes;  // one stage: kCons units of weights (+ their x fragments when staged)
-    float* cpart;     // chunk sums of split tiles: [tile][chunk of the tile][16 rows]
-    int* ticket;      // next dynamic chunk
     int* err;         // set when a bounded wait runs out
 };
 
@@ -1144,15 +1140,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 }
 
 // Shared-memory layout of the bulk kernel after the ring (the host sizes it
-// with the same arithmetic): the barriers full[S], empty[S], ready[2],
-// freed[2] and fin, the stages' chunk indices, two sets of per-warp partial
-// rows, a zero slot and the abort flag.
+// with the same arithmetic): the barriers full[S], empty[S], ready[2] and
+// freed[2] and fin, two ints of piece description per stage, two sets of
+// per-warp partial rows, a zero slot and the abort flag.
 __host__ __device__ constexpr size_t bulk_bars_off(int S, int stage_bytes) { return size_t(S) * stage_bytes; }
 __host__ __device__ constexpr size_t bulk_part_off(int S, int stage_bytes) {
-    return (bulk_bars_off(S, stage_bytes) + 8 * (2 * size_t(S) + 5) + 4 * size_t(S) + 15) & ~size_t(15);
+    return (bulk_bars_off(S, stage_bytes) + 8 * (2 * size_t(S) + 5) + 8 * size_t(S) + 15) & ~size_t(15);
 }
 __host__ __device__ constexpr size_t bulk_smem_bytes(int S, int stage_bytes) {
     return bulk_part_off(S, stage_bytes) + 2 * kCons * MMA_TILE_ROWS * sizeof(float) + kSlotBytes + 16;
+}
+
+// CTA of a grid of G whose unit range [c U / G, (c + 1) U / G) holds unit u.
+__device__ __forceinline__ int cta_of_unit(int64_t u, int64_t U, int G) {
+    return static_cast<int>(((u + 1) * G + U - 1) / U - 1);
 }
 
 template <int TYPE, bool kXS>
@@ -1162,15 +1163,17 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
     const int S = b.stages, SB = b.stage_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + bulk_bars_off(S, SB));
     uint64_t* empty = full + S;
-    uint64_t* ready = empty + S;  // [2]: the consumers' partial rows of a chunk are written
-    uint64_t* freed = ready + 2;  // [2]: the reducer has read them
+    uint64_t* ready = empty + S;  // [2]: the warps' partial rows of a tile are written
+    uint64_t* freed = ready + 2;  // [2]: every warp is done with those partial rows
     uint64_t* fin = freed + 2;    // every consumer warp has left its loop
-    int* s_chunk = reinterpret_cast<int*>(fin + 1);
+    int* s_meta = reinterpret_cast<int*>(fin + 1);  // per stage: first tile (-1: end), g0 | len << 16 | last << 31
     float* s_part = reinterpret_cast<float*>(smem + bulk_part_off(S, SB));
     uint32_t* s_zero = reinterpret_cast<uint32_t*>(s_part + 2 * kCons * MMA_TILE_ROWS);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_zero + kSlotBytes / 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int ng = static_cast<int>(a.ngroups);
+    const int G = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
+    const int64_t U = a.units, T = U / ng;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
@@ -1179,7 +1182,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(ready + i, kCons);
-            mbar_init(freed + i, 1);
+            mbar_init(freed + i, kCons);
         }
         mbar_init(fin, kCons);
         *s_abort = 0;
@@ -1195,73 +1198,80 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
     __syncthreads();
     pdl_release();
 
+    // this CTA's work: units [u0, u1) (split mode) or tiles [t0, t1) (whole-tile mode)
+    const int64_t u0 = b.whole ? (int64_t(cta) * T / G) * ng : int64_t(cta) * U / G;
+    const int64_t u1 = b.whole ? (int64_t(cta + 1) * T / G) * ng : int64_t(cta + 1) * U / G;
+
     if (warp == kCons) {
         // ------------------------------------------------------- producer
         if (lane != 0) return;
-        auto weights = [&](int c, int stage, bool arrive) -> uint32_t {
-            uint8_t* dst = smem + size_t(stage) * SB;
-            uint32_t bytes = 0;
-            s_chunk[stage] = c;
-            if (b.nck > 0) {
-                const int tile = c / b.nck, g0 = (c - tile * b.nck) * kCons;
-                const int gc = ng - g0 < kCons ? ng - g0 : kCons;
-                const SegRef sr = seg_ref(a, tile);
-                bytes = static_cast<uint32_t>(gc * UB);
-                if (arrive) mbar_arrive_tx(full + stage, bytes + (kXS ? gc * kGroupFragBytes : 0));
-                else mbar_expect_tx(full + stage, bytes);
-                bulk_g2s(dst, sr.W + ((int64_t(tile) - sr.first_tile) * ng + g0) * UB, bytes, full + stage);
-            } else {
-                const int t0 = c * b.tpc, nt = b.ntiles - t0 < b.tpc ? b.ntiles - t0 : b.tpc;
-                bytes = static_cast<uint32_t>(nt * ng * UB);
-                if (arrive) mbar_arrive_tx(full + stage, bytes + (kXS ? ng * kGroupFragBytes : 0));
-                else mbar_expect_tx(full + stage, bytes);
-                for (int j = 0; j < nt; ++j) {
-                    const SegRef sr = seg_ref(a, t0 + j);
-                    bulk_g2s(dst + j * ng * UB, sr.W + (int64_t(t0 + j) - sr.first_tile) * ng * UB,
-                             static_cast<uint32_t>(ng * UB), full + stage);
-                }
-            }
-            return bytes;
-        };
-        // x fragments of chunk c (staged-x variant): written by the previous
-        // launch or the x preparation, so only after the dependency wait
-        auto xfrags = [&](int c, int stage, bool arrive) {
-            const int g0 = b.nck > 0 ? (c % b.nck) * kCons : 0;
-            const int gc = b.nck > 0 ? (ng - g0 < kCons ? ng - g0 : kCons) : ng;
-            const uint32_t bytes = static_cast<uint32_t>(gc * kGroupFragBytes);
-            if (arrive) mbar_arrive_tx(full + stage, bytes);
-            bulk_g2s(smem + size_t(stage) * SB + kCons * UB, a.frags + int64_t(g0) * kGroupFragBytes, bytes,
-                     full + stage);
-        };
-        const int grid = static_cast<int>(gridDim.x);
         int it = 0;
-        for (; it < S; ++it) {  // the fixed chunks: weights only, before the dependency wait
-            const int c = static_cast<int>(blockIdx.x) + it * grid;
-            if (c >= b.nchunks) break;
-            weights(c, it, !kXS);
-        }
-        const int fixed = it;
-        pdl_wait();
-        if (kXS)
-            for (int i = 0; i < fixed; ++i) xfrags(static_cast<int>(blockIdx.x) + i * grid, i, true);
-        bool more = fixed == S;
-        while (more) {
-            const int c = S * grid + atomicAdd(b.ticket, 1);
+        bool waited = !kXS;  // only the staged-x copies depend on the previous kernel
+        // after the dependency wait: the x copies and arrivals of the first n
+        // pieces, whose weights were requested before it (staged-x variant)
+        auto after_wait = [&](int n) {
+            pdl_wait();
+            waited = true;
+            for (int i = 0; i < n; ++i) {
+                const int m = s_meta[2 * i + 1];
+                const int g0 = m & 0xFFFF, len = (m >> 16) & 0x7FFF;
+                const uint32_t xbytes = static_cast<uint32_t>((b.whole ? ng : len) * kGroupFragBytes);
+                mbar_arrive_tx(full + i, xbytes);
+                bulk_g2s(smem + size_t(i) * SB + kCons * UB, a.frags + int64_t(b.whole ? 0 : g0) * kGroupFragBytes,
+                         xbytes, full + i);
+            }
+        };
+        for (int64_t u = u0; u < u1; ++it) {
+            const int64_t tile = u / ng;
+            int len, g0 = static_cast<int>(u - tile * ng);
+            bool last;
+            if (b.whole) {
+                len = static_cast<int>(u1 - u < kCons ? u1 - u : kCons);  // whole tiles: kCons is a multiple of ng
+                last = true;
+            } else {
+                const int64_t tend = (tile + 1) * ng;
+                const int64_t e = tend < u1 ? tend : u1;
+                len = static_cast<int>(e - u < kCons ? e - u : kCons);
+                last = u + len == e;
+            }
             const int stage = it % S;
-            if (!mbar_wait(empty + stage, static_cast<uint32_t>((it / S) - 1) & 1u, s_abort)) {
+            if (it == S && !waited) after_wait(S);
+            if (it >= S && !mbar_wait(empty + stage, static_cast<uint32_t>((it / S) - 1) & 1u, s_abort)) {
                 atomicExch(b.err, 1);
                 *s_abort = 1;
                 return;
             }
-            if (c >= b.nchunks) break;
-            weights(c, stage, true);
-            if (kXS) xfrags(c, stage, false);
-            ++it;
+            s_meta[2 * stage] = static_cast<int>(tile);
+            s_meta[2 * stage + 1] = g0 | (len << 16) | (last ? int(0x80000000u) : 0);
+            uint8_t* dst = smem + size_t(stage) * SB;
+            const uint32_t wbytes = static_cast<uint32_t>(len * UB);
+            const uint32_t xbytes = kXS ? static_cast<uint32_t>((b.whole ? ng : len) * kGroupFragBytes) : 0u;
+            if (kXS && !waited) mbar_expect_tx(full + stage, wbytes);  // the x copy and the arrival come after the wait
+            else mbar_arrive_tx(full + stage, wbytes + xbytes);
+            // a piece's units are contiguous in memory unless it spans two matrices (whole-tile mode)
+            int done = 0;
+            while (done < len) {
+                const int64_t tt = (u + done) / ng;
+                const SegRef sr = seg_ref(a, tt);
+                const int64_t seg_end_u = sr.end_tile * ng;
+                const int n = static_cast<int>(u + len < seg_end_u ? len - done : seg_end_u - (u + done));
+                bulk_g2s(dst + done * UB, sr.W + ((tt - sr.first_tile) * ng + (u + done - tt * ng)) * UB,
+                         static_cast<uint32_t>(n * UB), full + stage);
+                done += n;
+            }
+            if (kXS && waited)
+                bulk_g2s(dst + kCons * UB, a.frags + int64_t(b.whole ? 0 : g0) * kGroupFragBytes, xbytes, full + stage);
+            u += len;
         }
-        // end of the work: a stage whose chunk index is -1 (its previous use,
-        // if any, was released above)
+        if (!waited) after_wait(it);
+        // end of the work: a stage whose tile is -1 (its previous use was released above)
         const int stage = it % S;
-        s_chunk[stage] = -1;
+        if (it >= S && !mbar_wait(empty + stage, static_cast<uint32_t>((it / S) - 1) & 1u, s_abort)) {
+            atomicExch(b.err, 1);
+            *s_abort = 1;
+            return;
+        }
+        s_meta[2 * stage] = -1;
         mbar_arrive(full + stage);
         return;
     }
@@ -1276,126 +1286,115 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
     }
     const int ctid = warp * 32 + lane;
     if (a.f_bl != 0) {
-        const int64_t gt = int64_t(blockIdx.x) * (kCons * 32) + ctid;
-        for (int64_t i = gt; i < a.f_ncount; i += int64_t(gridDim.x) * (kCons * 32)) a.f_count[i] = 0;
+        const int64_t gt = int64_t(cta) * (kCons * 32) + ctid;
+        for (int64_t i = gt; i < a.f_ncount; i += int64_t(G) * (kCons * 32)) a.f_count[i] = 0;
         if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
     }
     const bool supplier = g == t || g == t + 4;
     const int fc = supplier ? kChunkFragBytes : 0;
+    const int64_t first_tile = u0 / ng;
     bool ok = true;
-    for (int it = 0;; ++it) {
-        const int stage = it % S, par = it & 1;
+    float y0 = 0.f, y8 = 0.f;
+    for (int it = 0, flush = 0;; ++it) {
+        const int stage = it % S;
         if (!mbar_wait(full + stage, static_cast<uint32_t>(it / S) & 1u, s_abort)) {
             ok = false;
             break;
         }
-        const int c = s_chunk[stage];
-        if (c < 0) break;
-        int tile, gi, gc, k = 0;
-        if (b.nck > 0) {
-            tile = c / b.nck;
-            k = c - tile * b.nck;
-            gi = k * kCons + warp;
-            gc = ng - k * kCons < kCons ? ng - k * kCons : kCons;
-        } else {
-            tile = c * b.tpc + warp / ng;
-            gi = warp % ng;
-            gc = (b.ntiles - c * b.tpc < b.tpc ? b.ntiles - c * b.tpc : b.tpc) * ng;
-        }
-        float y0 = 0.f, y8 = 0.f;
-        if (warp < gc) {
+        const int tile0 = s_meta[2 * stage];
+        if (tile0 < 0) break;
+        const int m = s_meta[2 * stage + 1];
+        const int g0 = m & 0xFFFF, len = (m >> 16) & 0x7FFF;
+        const bool last = m < 0;
+        if (warp < len) {
             const uint8_t* st = smem + size_t(stage) * SB;
+            const int gi = b.whole ? warp % ng : g0 + warp;
             const uint8_t* fb;
             if constexpr (kXS)
-                fb = supplier ? st + kCons * UB + (b.nck > 0 ? warp : gi) * kGroupFragBytes + g * kSlotBytes
+                fb = supplier ? st + kCons * UB + (b.whole ? gi : warp) * kGroupFragBytes + g * kSlotBytes
                               : reinterpret_cast<const uint8_t*>(s_zero);
             else
                 fb = supplier ? a.frags + int64_t(gi) * kGroupFragBytes + g * kSlotBytes : a.zeros;
             group_dot<TYPE, LdShared, typename std::conditional<kXS, LdShared, LdGlobal>::type>(
                 st + warp * UB, fb, fc, a.scale + int64_t(gi) * kXBlocks<TYPE>, a.xsum + int64_t(gi) * kXBlocks<TYPE>,
                 lane, g, t, y0, y8);
-            y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
-            y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
-            y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
-            y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + stage);  // this warp is done with the stage
-        // partial rows of this chunk: the buffer of this parity was last read
-        // by the reducer two chunks ago
-        if (it >= 2 && !mbar_wait(freed + par, static_cast<uint32_t>((it >> 1) - 1) & 1u, s_abort)) {
+        if (!last) continue;
+        // ---- flush: the tile(s) of this piece end here for this CTA
+        const int par = flush & 1;
+        if (flush >= 2 && !mbar_wait(freed + par, static_cast<uint32_t>((flush >> 1) - 1) & 1u, s_abort)) {
             ok = false;
             break;
         }
         float* part = s_part + par * kCons * MMA_TILE_ROWS;
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
+        y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
+        y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
+        y8 += __shfl_xor_sync(0xffffffffu, y8, 2);
         if (t == 0) {
             part[warp * MMA_TILE_ROWS + g] = y0;
             part[warp * MMA_TILE_ROWS + g + 8] = y8;
         }
+        y0 = y8 = 0.f;
         __syncwarp();
         if (lane == 0) mbar_arrive(ready + par);
-        if (warp != c % kCons) continue;
-        // this warp reduces the chunk: add the warps' partial rows in warp order
-        if (!mbar_wait(ready + par, static_cast<uint32_t>(it >> 1) & 1u, s_abort)) {
-            ok = false;
-            break;
-        }
         const int r = lane & 15;
-        if (b.nck > 0) {
-            float acc = 0.f;
-            for (int v = 0; v < gc; ++v) acc += part[v * MMA_TILE_ROWS + r];
-            __syncwarp();
-            if (lane == 0) mbar_arrive(freed + par);
-            const SegRef sr = seg_ref(a, tile);
-            float* ty = sr.y + (int64_t(tile) - sr.first_tile) * MMA_TILE_ROWS;
-            bool emitted = false;
-            if (b.nck == 1) {
-                if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, acc, hoff);
-                emitted = true;
-            } else {
-                float* slots = b.cpart + int64_t(tile) * b.nck * MMA_TILE_ROWS;
-                if (lane < MMA_TILE_ROWS) slots[k * MMA_TILE_ROWS + r] = acc;
-                __threadfence();
-                __syncwarp();
-                int prev = 0;
-                if (lane == 0) prev = atomicAdd(a.count + tile, 1);
-                prev = __shfl_sync(0xffffffffu, prev, 0);
-                if (prev == b.nck - 1) {  // the tile's last chunk: add the chunk sums in chunk order
-                    __threadfence();
-                    float sum = 0.f;
-                    if (lane < MMA_TILE_ROWS)
-                        for (int kk = 0; kk < b.nck; ++kk) sum += __ldcg(slots + kk * MMA_TILE_ROWS + r);
-                    if (lane < MMA_TILE_ROWS) emit(a, ty, tile, r, sum, hoff);
-                    emitted = true;
-                }
+        const int ntc = b.whole ? (len + ng - 1) / ng : 1;  // tiles ending in this piece
+        const int reducer = b.whole ? -1 : tile0 % kCons;
+        float acc = 0.f;
+        int my_tile = -1;  // the tile this warp reduces
+        if (b.whole) {
+            if (warp % ng == 0 && warp / ng < ntc) my_tile = tile0 + warp / ng;
+        } else if (warp == reducer) {
+            my_tile = tile0;
+        }
+        if (my_tile >= 0) {
+            if (!mbar_wait(ready + par, static_cast<uint32_t>(flush >> 1) & 1u, s_abort)) {
+                ok = false;
+                break;
             }
-            if (emitted && a.f_bl != 0 && tile >= a.f_t0 && tile < a.f_t1)
-                feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl,
-                          lane);
+            const int w0 = b.whole ? warp : 0, wn = b.whole ? ng : kCons;
+            for (int v = w0; v < w0 + wn; ++v) acc += part[v * MMA_TILE_ROWS + r];  // warp order
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(freed + par);
+        ++flush;
+        if (my_tile < 0) continue;
+        const SegRef sr = seg_ref(a, my_tile);
+        float* ty = sr.y + (int64_t(my_tile) - sr.first_tile) * MMA_TILE_ROWS;
+        bool emitted = false;
+        const int64_t ts = int64_t(my_tile) * ng;
+        if (b.whole || (ts >= u0 && ts + ng <= u1)) {  // the whole tile was this CTA's
+            if (lane < MMA_TILE_ROWS) emit(a, ty, my_tile, r, acc, hoff);
+            emitted = true;
         } else {
-            // whole tiles: tile j of the chunk is warps j ng .. j ng + ng - 1
-            const int ntc = gc / ng;
-            float acc[kCons];
-#pragma unroll
-            for (int j = 0; j < kCons; ++j) {
-                acc[j] = 0.f;
-                if (j < ntc)
-                    for (int v = 0; v < ng; ++v) acc[j] += part[(j * ng + v) * MMA_TILE_ROWS + r];
-            }
+            // shared with neighbouring CTAs: the CTA's sum to its slot (0: its
+            // first tile, 1: its last); the last CTA adds them in CTA order
+            const int ca = cta_of_unit(ts, U, G), cb = cta_of_unit(ts + ng - 1, U, G);
+            if (lane < MMA_TILE_ROWS)
+                a.partial[(cta * 2 + (my_tile == first_tile ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
+            __threadfence();
             __syncwarp();
-            if (lane == 0) mbar_arrive(freed + par);
-#pragma unroll
-            for (int j = 0; j < kCons; ++j) {
-                if (j >= ntc) break;
-                const int tj = c * b.tpc + j;
-                const SegRef sr = seg_ref(a, tj);
-                float* ty = sr.y + (int64_t(tj) - sr.first_tile) * MMA_TILE_ROWS;
-                if (lane < MMA_TILE_ROWS) emit(a, ty, tj, r, acc[j], hoff);
-                if (a.f_bl != 0 && tj >= a.f_t0 && tj < a.f_t1)
-                    feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tj - a.f_t0), a.f_bl,
-                              lane);
+            int prev = 0;
+            if (lane == 0) prev = atomicAdd(a.count + my_tile, 1);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == cb - ca) {
+                __threadfence();
+                float sum = 0.f;
+                if (lane < MMA_TILE_ROWS)
+                    for (int c2 = ca; c2 <= cb; ++c2) {
+                        const int64_t ft = (int64_t(c2) * U / G) / ng;  // CTA c2's first tile
+                        sum += __ldcg(a.partial + (c2 * 2 + (ft == my_tile ? 0 : 1)) * MMA_TILE_ROWS + r);
+                    }
+                if (lane < MMA_TILE_ROWS) emit(a, ty, my_tile, r, sum, hoff);
+                emitted = true;
             }
         }
+        if (emitted && a.f_bl != 0 && my_tile >= a.f_t0 && my_tile < a.f_t1)
+            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(my_tile - a.f_t0), a.f_bl,
+                      lane);
     }
     if (!ok) {
         if (lane == 0) atomicExch(b.err, 1);
@@ -1414,7 +1413,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
                 return;
             }
             __threadfence();
-            if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
+            if (atomicAdd(a.done, 1) == G - 1) {
                 __threadfence_system();
                 for (int p = 0; p < a.x.world; ++p)
                     if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, xe);
@@ -1634,19 +1633,10 @@ static int sm_count() {
 }
 
 // Counters of a launch over `ntiles` tiles: one per tile, the CTA completion
-// counter, one per 32-value chunk of an output that feeds the next launch,
-// and the bulk kernel's chunk ticket (the last one).  All start at zero:
-// cleared by the x-preparation kernel, or by the launch before when that one
-// prepares x.
-static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1 + 1; }
-
-// Chunk sums of the bulk kernel's split tiles, after the layout above:
-// [tile][chunk of the tile][16 rows] floats.
-static size_t bulk_cpart_bytes(int64_t N, int64_t K) {
-    const int64_t ng = K / 256;
-    return ng > kCons ? size_t(N / MMA_TILE_ROWS) * size_t((ng + kCons - 1) / kCons) * MMA_TILE_ROWS * sizeof(float)
-                      : 0;
-}
+// counter, and one per 32-value chunk of an output that feeds the next launch.
+// All start at zero: cleared by the x-preparation kernel, or by the launch
+// before when that one prepares x.
+static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1; }
 
 // Scratch of one MMA GEMV launch (layout described above the kernels).
 ScratchLayout scratch_layout(int64_t N, int64_t K) {
@@ -1666,7 +1656,7 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
 
 size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
-size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total + bulk_cpart_bytes(N, K); }
+size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
 // Which GEMV kernel serves MMA-layout launches: XDNA_B200_GEMV = "classic"
 // (gemv_mma_kernel), "bulk" (gemv_bulk_kernel, x fragments through the L1) or
@@ -1709,8 +1699,8 @@ cudaError_t gemv_error_status(int* out) {
 }
 
 // Launch plan of the bulk kernel for one launch, or false where it does not
-// apply (a tile count of groups that neither fills a chunk nor divides kCons,
-// or no room for two stages).
+// apply (a tile group count below kCons that does not divide it, or no room
+// for two stages).
 struct BulkPlan {
     BulkArgs b;
     int grid;
@@ -1724,27 +1714,25 @@ static bool bulk_plan(bool staged_x, int64_t ngroups, int64_t ntiles, int sms, B
     const size_t budget = 227 * 1024 - kGrid - 1024;
     BulkArgs& b = p->b;
     b = BulkArgs{};
+    int64_t work;  // the units (split mode) or tiles (whole-tile mode) shared among the CTAs
+    if (ngroups >= 32768) return false;  // a piece's first group is kept in 16 bits
     if (ngroups >= kCons) {
-        b.nck = static_cast<int>((ngroups + kCons - 1) / kCons);
-        b.tpc = 0;
-        if (ntiles * b.nck >= (int64_t(1) << 31)) return false;
-        b.nchunks = static_cast<int>(ntiles * b.nck);
+        b.whole = 0;
+        work = ntiles * ngroups;
     } else if (ngroups > 0 && kCons % ngroups == 0) {
-        b.nck = 0;
-        b.tpc = static_cast<int>(kCons / ngroups);
-        b.nchunks = static_cast<int>((ntiles + b.tpc - 1) / b.tpc);
+        b.whole = 1;
+        work = ntiles;
     } else {
         return false;
     }
-    b.ntiles = static_cast<int>(ntiles);
     b.stage_bytes = ((kCons * UB + (staged_x ? kCons * kGroupFragBytes : 0)) + 127) & ~127;
     int S = 8;
     while (S >= 2 && bulk_smem_bytes(S, b.stage_bytes) > budget) --S;
     if (S < 2) return false;
     b.stages = S;
     p->smem = bulk_smem_bytes(S, b.stage_bytes);
-    p->grid = b.nchunks < sms ? b.nchunks : sms;
-    return true;
+    p->grid = static_cast<int>(work < sms ? work : sms);
+    return p->grid <= kMaxCtas;
 }
 
 template <int TYPE, bool kXS>
@@ -1758,6 +1746,15 @@ static cudaError_t launch_bulk_typed(cudaLaunchConfig_t& cg, const GemvArgs& a, 
         e = cudaFuncSetAttribute(gemv_bulk_kernel<TYPE, kXS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(cg.dynamicSmemBytes));
         if (e != cudaSuccess) return e;
+        // the kernels that run between bulk GEMVs take the same shared-memory
+        // carve-out, so that an SM need not drain to switch it and the
+        // programmatic-launch overlap is kept
+        for (const void* f : {reinterpret_cast<const void*>(xprep_kernel<16>),
+                              reinterpret_cast<const void*>(xprep_kernel<32>),
+                              reinterpret_cast<const void*>(xchg_gather_kernel)}) {
+            e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+            if (e != cudaSuccess) return e;
+        }
         smem_set[dev].store(cg.dynamicSmemBytes);
     }
     return cudaLaunchKernelEx(&cg, gemv_bulk_kernel<TYPE, kXS>, a, b);
@@ -1765,8 +1762,8 @@ static cudaError_t launch_bulk_typed(cudaLaunchConfig_t& cg, const GemvArgs& a, 
 
 // Plans and launches the bulk kernel for `type`; *used = false (nothing
 // launched) where it does not apply.
-static cudaError_t launch_bulk(int type, bool staged_x, const GemvArgs& a, int64_t ntiles, int sms, uint8_t* base,
-                               const ScratchLayout& L, cudaStream_t stream, bool* used) {
+static cudaError_t launch_bulk(int type, bool staged_x, const GemvArgs& a, int64_t ntiles, int sms,
+                               cudaStream_t stream, bool* used) {
     BulkPlan p;
     bool ok = false;
     switch (type) {
@@ -1782,8 +1779,6 @@ static cudaError_t launch_bulk(int type, bool staged_x, const GemvArgs& a, int64
     }
     *used = false;
     if (!ok) return cudaSuccess;
-    p.b.cpart = reinterpret_cast<float*>(base + L.total);
-    p.b.ticket = a.count + counter_ints(ntiles) - 1;
     p.b.err = gemv_err_ptr();
     if (!p.b.err) return cudaErrorInvalidDevice;
     cudaLaunchConfig_t cg = {};
@@ -1987,7 +1982,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     const int choice = classic ? 0 : gemv_kernel_choice();
     if (choice != 0) {
         bool used = false;
-        const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, base, L, stream, &used);
+        const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, stream, &used);
         if (used || e != cudaSuccess) return e;
     }
     cudaLaunchConfig_t cg = {};
