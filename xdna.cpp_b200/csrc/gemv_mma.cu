@@ -243,6 +243,7 @@ struct GemvArgs {
     int* f_count;       // the next launch's counters (f_ncount ints) and zero slot, cleared here
     int64_t f_ncount;
     uint32_t* f_zeros;
+    int* err;           // set when a bounded wait (shared-memory ring) runs out
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -863,6 +864,68 @@ __device__ __forceinline__ void group_dot(const uint8_t* gb, const uint8_t* fb, 
         group_dot_nib<TYPE, W, X>(gb, fb, fc, sc_, xs_, lane, g, t, y0, y8);
 }
 
+// Bounded waits of the shared-memory rings: 2 s of %globaltimer.
+constexpr uint64_t kBulkWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bounded wait for the completion of the barrier phase with parity `parity`;
+// false when it runs out or *abort (if given) is set.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
+    const uint32_t addr = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255u) == 0) {
+            const uint64_t now = global_ns();
+            if (i == 0) t0 = now;
+            else if ((abort && *abort) || now - t0 > kBulkWaitNs) return false;
+        }
+    }
+}
+// Global -> shared bulk copy completing on `bar` (16-byte aligned, bytes a multiple of 16).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Per-warp shared-memory ring of gemv_mma_kernel's ring variant: depth (in
+// units) per format, sized so that the 24 warps' rings take about 170 KiB.
+template <int TYPE>
+constexpr int kRingDepth = (170 * 1024) / (kWarps * kUnitBytes<TYPE>) > 4 ? 4
+                                                                        : (170 * 1024) / (kWarps * kUnitBytes<TYPE>);
+// Bytes of the ring variant's dynamic shared memory after the partial rows
+// and tile counters (offset `off`): the rings, then their barriers.
+template <int TYPE>
+constexpr size_t ring_bytes() {
+    return size_t(kWarps) * kRingDepth<TYPE> * kUnitBytes<TYPE> + size_t(kWarps) * kRingDepth<TYPE> * 8;
+}
+__host__ __device__ constexpr size_t ring_offset(int cta_tiles) {
+    return (size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(cta_tiles) * sizeof(int) + 127) & ~size_t(127);
+}
+
 // After a warp has written all 16 rows of `tile`: if the tile feeds the next
 // launch, count it in at its 32-value chunk; the second of the chunk's two
 // tiles (in any CTA) prepares the chunk as the x-preparation kernel would.
@@ -886,8 +949,13 @@ __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum
 }
 
 // kTiles: tile mode (a compile-time choice, so the unit-mode kernel carries
-// none of its code)
-template <int TYPE, bool kTiles>
+// none of its code).  kRing: the weights reach each warp through its own
+// shared-memory ring instead of streaming loads: lane 0 requests the warp's
+// next units with bulk copies (cp.async.bulk, completing on one mbarrier per
+// slot) kRingDepth units ahead, the first ones before the programmatic-launch
+// wait, and the warp reads each unit from shared memory once its barrier
+// completes.  Everything else (split, combine, epilogue) is the same.
+template <int TYPE, bool kTiles, bool kRing = false>
 __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(const GemvArgs a) {
     // unit, tile and group counts fit in 32 bits (the launcher checks)
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -898,11 +966,27 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     const int u1 = kTiles ? sp.warp_unit0(w + 1) : (w < NW ? static_cast<int>(int64_t(w + 1) * U / NW) : 0);
     // shared memory: per-warp partial rows (2 slots) and one arrival counter
     // per tile this CTA touches, counted from t0, the tile of its first unit
-    extern __shared__ __align__(16) float s_part[];
+    extern __shared__ __align__(128) float s_part[];
     int* s_count = reinterpret_cast<int*>(s_part + kWarps * 2 * MMA_TILE_ROWS);
     const int t0 = kTiles ? sp.cta_unit0(static_cast<int>(blockIdx.x)) / ng
                           : static_cast<int>(int64_t(blockIdx.x) * kWarps * U / NW) / ng;
     for (int i = threadIdx.x; i < a.cta_tiles; i += blockDim.x) s_count[i] = 0;
+    constexpr int UB = kUnitBytes<TYPE>;
+    constexpr int D = kRing ? kRingDepth<TYPE> : 1;
+    __shared__ int s_abort;
+    uint8_t* ring = nullptr;
+    uint64_t* rbar = nullptr;
+    if constexpr (kRing) {
+        uint8_t* rb = reinterpret_cast<uint8_t*>(s_part) + ring_offset(a.cta_tiles);
+        const int wi = threadIdx.x >> 5;
+        ring = rb + size_t(wi) * D * UB;
+        rbar = reinterpret_cast<uint64_t*>(rb + size_t(kWarps) * D * UB) + wi * D;
+        if (lane == 0) {
+            for (int i = 0; i < D; ++i) mbar_init(rbar + i, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        if (threadIdx.x == 0) s_abort = 0;
+    }
     if constexpr (TYPE == T_IQ3_S)
         for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
     if constexpr (TYPE == T_IQ3_XXS)
@@ -910,10 +994,35 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     if constexpr (TYPE == T_IQ2_S)
         for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s_grid[i] = kIq2sGrid[i];
     __syncthreads();
-    // start this warp's first weights towards L2 before waiting on xprep
-    if (lane == 0)
-        for (int d = 0; d < kPrefetch && u0 + d < u1; ++d)
-            prefetch_l2(unit_weights<TYPE>(a, u0 + d), kUnitBytes<TYPE>);
+    // fetch cursor of the ring (lane 0): the next unit to request, its
+    // address, and the units left in its matrix from there on
+    int fu = u0;
+    const uint8_t* faddr = nullptr;
+    int fleft = 0;
+    auto request = [&](int slot) {
+        if (fleft == 0) {
+            const int ft = fu / ng;
+            const SegRef sr = seg_ref(a, ft);
+            faddr = sr.W + (int64_t(ft - static_cast<int>(sr.first_tile)) * ng + (fu - ft * ng)) * UB;
+            fleft = static_cast<int>(sr.end_tile) * ng - fu;
+        }
+        mbar_arrive_tx(rbar + slot, UB);
+        bulk_g2s(ring + slot * UB, faddr, UB, rbar + slot);
+        if (fleft > 3) prefetch_l2(faddr + 3 * UB, UB);  // keep DRAM a few units ahead of the copies
+        ++fu;
+        faddr += UB;
+        --fleft;
+    };
+    if constexpr (kRing) {
+        // the warp's first units: weights are never written by the kernels this one overlaps
+        if (lane == 0)
+            for (int d = 0; d < D && fu < u1; ++d) request(d);
+    } else {
+        // start this warp's first weights towards L2 before waiting on xprep
+        if (lane == 0)
+            for (int d = 0; d < kPrefetch && u0 + d < u1; ++d)
+                prefetch_l2(unit_weights<TYPE>(a, u0 + d), kUnitBytes<TYPE>);
+    }
     pdl_release();
     pdl_wait();  // x digits and the zeroed tile counters come from xprep_kernel (or the previous launch)
     uint32_t xe = 0;  // sharded: this launch's epoch and exchange data half
@@ -935,6 +1044,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
     const int fc = supplier ? kChunkFragBytes : 0;
     const int fg = supplier ? kGroupFragBytes : 0;
     int u = u0;
+    int j = 0;  // units this warp has consumed (ring slot and phase)
+    bool ok = true;
     while (u < u1) {
         const int tile = u / ng, tbeg = tile * ng;
         const int gend = (u1 - tbeg) < ng ? (u1 - tbeg) : ng;
@@ -947,11 +1058,25 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         }
         float y0 = 0.f, y8 = 0.f;
         for (int gi = u - tbeg; gi < gend; ++gi) {
-            if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
-                prefetch_l2(tw + (gi + kPrefetch) * kUnitBytes<TYPE>, kUnitBytes<TYPE>);
-            group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
-                            a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
+            if constexpr (kRing) {
+                const int slot = j % D;
+                if (!mbar_wait(rbar + slot, static_cast<uint32_t>(j / D) & 1u, &s_abort)) {
+                    ok = false;
+                    break;
+                }
+                group_dot<TYPE, LdShared, LdGlobal>(ring + slot * UB, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
+                                                    a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
+                __syncwarp();  // every lane has read the slot: refill it
+                if (lane == 0 && fu < u1) request(slot);
+                ++j;
+            } else {
+                if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
+                    prefetch_l2(tw + (gi + kPrefetch) * kUnitBytes<TYPE>, kUnitBytes<TYPE>);
+                group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
+                                a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
+            }
         }
+        if (!ok) break;
         y0 += __shfl_xor_sync(0xffffffffu, y0, 1);
         y0 += __shfl_xor_sync(0xffffffffu, y0, 2);
         y8 += __shfl_xor_sync(0xffffffffu, y8, 1);
@@ -1036,6 +1161,19 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl, lane);
         u = tbeg + gend;
     }
+    if constexpr (kRing) {
+        if (!ok) {
+            // a ring wait ran out (never expected): report it, let the copies
+            // still in flight into this warp's slots land (bounded), and leave
+            // this launch's outputs incomplete rather than hang
+            if (lane == 0) {
+                atomicExch(a.err, 1);
+                s_abort = 1;
+                for (int k = j; k < fu - u0; ++k) mbar_wait(rbar + k % D, static_cast<uint32_t>(k / D) & 1u, nullptr);
+            }
+            __syncwarp();
+        }
+    }
     if (a.xchg) {
         // Every row this CTA stored (locally and into the peers' buffers) is
         // ordered before its count-in at device scope; the last CTA to count
@@ -1087,7 +1225,6 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
 // ---------------------------------------------------------------------------
 constexpr int kCons = 16;
 constexpr int kBulkThreads = (kCons + 1) * 32;
-constexpr uint64_t kBulkWaitNs = 2000000000ull;
 
 struct BulkArgs {
     int whole;        // whole-tile mode
@@ -1095,49 +1232,6 @@ struct BulkArgs {
     int stage_bytes;  // one stage: kCons units of weights (+ their x fragments when staged)
     int* err;         // set when a bounded wait runs out
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-// Bounded wait for the completion of the barrier phase with parity `parity`.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const volatile int* abort) {
-    const uint32_t addr = smem_u32(bar);
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if ((i & 255u) == 0) {
-            const uint64_t now = global_ns();
-            if (i == 0) t0 = now;
-            else if (*abort || now - t0 > kBulkWaitNs) return false;
-        }
-    }
-}
-// Global -> shared bulk copy completing on `bar` (16-byte aligned, bytes a multiple of 16).
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
 
 // Shared-memory layout of the bulk kernel after the ring (the host sizes it
 // with the same arithmetic): the barriers full[S], empty[S], ready[2] and
@@ -1659,15 +1753,17 @@ size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
 // Which GEMV kernel serves MMA-layout launches: XDNA_B200_GEMV = "classic"
-// (gemv_mma_kernel), "bulk" (gemv_bulk_kernel, x fragments through the L1) or
-// "bulkx" (gemv_bulk_kernel with the x fragments staged beside the weights).
-// Read once per process.
+// (gemv_mma_kernel with streaming loads), "ring" (gemv_mma_kernel with a
+// per-warp shared-memory ring), "bulk" (gemv_bulk_kernel, x fragments through
+// the L1) or "bulkx" (gemv_bulk_kernel with the x fragments staged beside the
+// weights).  Read once per process.
 static int gemv_kernel_choice() {
     static const int choice = [] {
         const char* v = getenv("XDNA_B200_GEMV");
         if (v && !strcmp(v, "classic")) return 0;
+        if (v && !strcmp(v, "bulk")) return 1;
         if (v && !strcmp(v, "bulkx")) return 2;
-        return 1;
+        return 3;
     }();
     return choice;
 }
@@ -1696,6 +1792,19 @@ cudaError_t gemv_error_status(int* out) {
     if (e == cudaSuccess && v) e = cudaMemset(p, 0, sizeof(int));
     *out = v;
     return e;
+}
+
+// The kernels that run between GEMVs (x preparation, gather) take the
+// shared-memory carve-out of the large-shared-memory GEMV variants, so that an
+// SM need not drain to switch it and the programmatic-launch overlap is kept.
+static cudaError_t match_carveouts() {
+    for (const void* f : {reinterpret_cast<const void*>(xprep_kernel<16>), reinterpret_cast<const void*>(xprep_kernel<32>),
+                          reinterpret_cast<const void*>(xchg_gather_kernel)}) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // Launch plan of the bulk kernel for one launch, or false where it does not
@@ -1745,16 +1854,8 @@ static cudaError_t launch_bulk_typed(cudaLaunchConfig_t& cg, const GemvArgs& a, 
     if (smem_set[dev].load() < cg.dynamicSmemBytes) {
         e = cudaFuncSetAttribute(gemv_bulk_kernel<TYPE, kXS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(cg.dynamicSmemBytes));
+        if (e == cudaSuccess) e = match_carveouts();
         if (e != cudaSuccess) return e;
-        // the kernels that run between bulk GEMVs take the same shared-memory
-        // carve-out, so that an SM need not drain to switch it and the
-        // programmatic-launch overlap is kept
-        for (const void* f : {reinterpret_cast<const void*>(xprep_kernel<16>),
-                              reinterpret_cast<const void*>(xprep_kernel<32>),
-                              reinterpret_cast<const void*>(xchg_gather_kernel)}) {
-            e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-            if (e != cudaSuccess) return e;
-        }
         smem_set[dev].store(cg.dynamicSmemBytes);
     }
     return cudaLaunchKernelEx(&cg, gemv_bulk_kernel<TYPE, kXS>, a, b);
@@ -1851,18 +1952,57 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
     return cudaGetLastError();
 }
 
-template <bool kTiles>
+template <int TYPE, bool kTiles, bool kRing>
+static cudaError_t launch_gemv_typed(cudaLaunchConfig_t& cg, const GemvArgs& a) {
+    if constexpr (kRing) {
+        static std::atomic<size_t> smem_set[kMaxDevices];
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+        if (smem_set[dev].load() < cg.dynamicSmemBytes) {
+            e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, kTiles, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(cg.dynamicSmemBytes));
+            if (e == cudaSuccess) e = match_carveouts();
+            if (e != cudaSuccess) return e;
+            smem_set[dev].store(cg.dynamicSmemBytes);
+        }
+    }
+    return cudaLaunchKernelEx(&cg, gemv_mma_kernel<TYPE, kTiles, kRing>, a);
+}
+
+// Dynamic shared memory of gemv_mma_kernel for a launch touching cta_tiles
+// tiles per CTA (the ring variant adds its rings and barriers).
+static size_t gemv_smem(int type, int cta_tiles, bool ring) {
+    const size_t base = size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(cta_tiles) * sizeof(int);
+    if (!ring) return base;
+    size_t rb;
+    switch (type) {
+        case T_Q4_K: rb = ring_bytes<T_Q4_K>(); break;
+        case T_Q5_K: rb = ring_bytes<T_Q5_K>(); break;
+        case T_Q6_K: rb = ring_bytes<T_Q6_K>(); break;
+        case T_Q3_K: rb = ring_bytes<T_Q3_K>(); break;
+        case T_IQ4_XS: rb = ring_bytes<T_IQ4_XS>(); break;
+        case T_IQ3_S: rb = ring_bytes<T_IQ3_S>(); break;
+        case T_IQ3_XXS: rb = ring_bytes<T_IQ3_XXS>(); break;
+        case T_IQ2_S: rb = ring_bytes<T_IQ2_S>(); break;
+        default: rb = ring_bytes<T_Q4_0>(); break;
+    }
+    return ring_offset(cta_tiles) + rb;
+}
+
+template <bool kTiles, bool kRing>
 static cudaError_t launch_gemv(int type, cudaLaunchConfig_t& cg, const GemvArgs& a) {
     switch (type) {
-        case T_Q4_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_K, kTiles>, a);
-        case T_Q5_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q5_K, kTiles>, a);
-        case T_Q6_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q6_K, kTiles>, a);
-        case T_Q3_K: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q3_K, kTiles>, a);
-        case T_IQ4_XS: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ4_XS, kTiles>, a);
-        case T_IQ3_S: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ3_S, kTiles>, a);
-        case T_IQ3_XXS: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ3_XXS, kTiles>, a);
-        case T_IQ2_S: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_IQ2_S, kTiles>, a);
-        default: return cudaLaunchKernelEx(&cg, gemv_mma_kernel<T_Q4_0, kTiles>, a);
+        case T_Q4_K: return launch_gemv_typed<T_Q4_K, kTiles, kRing>(cg, a);
+        case T_Q5_K: return launch_gemv_typed<T_Q5_K, kTiles, kRing>(cg, a);
+        case T_Q6_K: return launch_gemv_typed<T_Q6_K, kTiles, kRing>(cg, a);
+        case T_Q3_K: return launch_gemv_typed<T_Q3_K, kTiles, kRing>(cg, a);
+        case T_IQ4_XS: return launch_gemv_typed<T_IQ4_XS, kTiles, kRing>(cg, a);
+        case T_IQ3_S: return launch_gemv_typed<T_IQ3_S, kTiles, kRing>(cg, a);
+        case T_IQ3_XXS: return launch_gemv_typed<T_IQ3_XXS, kTiles, kRing>(cg, a);
+        case T_IQ2_S: return launch_gemv_typed<T_IQ2_S, kTiles, kRing>(cg, a);
+        default: return launch_gemv_typed<T_Q4_0, kTiles, kRing>(cg, a);
     }
 }
 
@@ -1980,23 +2120,26 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     }
 
     const int choice = classic ? 0 : gemv_kernel_choice();
-    if (choice != 0) {
+    if (choice == 1 || choice == 2) {
         bool used = false;
         const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, stream, &used);
         if (used || e != cudaSuccess) return e;
     }
+    const bool ring = choice == 3;
+    a.err = gemv_err_ptr();
+    if (!a.err) return cudaErrorInvalidDevice;
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks));
     cg.blockDim = dim3(kGemvThreads);
-    cg.dynamicSmemBytes = smem;
+    cg.dynamicSmemBytes = gemv_smem(type, a.cta_tiles, ring);
     cg.stream = stream;
     cudaLaunchAttribute attr2[1];
     attr2[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr2[0].val.programmaticStreamSerializationAllowed = 1;  // overlap the L2 warm-up with xprep
     cg.attrs = attr2;
     cg.numAttrs = 1;
-    if (a.tile_mode) return launch_gemv<true>(type, cg, a);
-    return launch_gemv<false>(type, cg, a);
+    if (ring) return a.tile_mode ? launch_gemv<true, true>(type, cg, a) : launch_gemv<false, true>(type, cg, a);
+    return a.tile_mode ? launch_gemv<true, false>(type, cg, a) : launch_gemv<false, false>(type, cg, a);
 }
 
 cudaError_t xchg_gather_launch(const float* xdata, int64_t half_floats, const uint32_t* flags,
