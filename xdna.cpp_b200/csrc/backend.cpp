@@ -320,7 +320,9 @@ struct Backend {
         char* peer[kMaxPeers] = {};
         size_t cap_floats = 0;  // floats per data half
         uint32_t* epoch = nullptr;  // the device epoch counter (a word of the local flag region)
-        int* err = nullptr;     // set by a gather kernel whose wait timed out
+        int* err = nullptr;     // set by a gather kernel or a GEMV whose wait for the peers timed out
+        size_t slot_bytes = 0;  // the two x-scratch slots after the data halves (same offsets on every rank)
+        float** base_table = nullptr;  // device: each rank's data half 0 (ShardChain::peer_base)
     } xg;
     // CUDA graph of the last node list seen twice in a row with every operand
     // on this device (see compute_graph); scratch_gen invalidates it when the
@@ -337,6 +339,12 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K);
 // Both x-scratch slots hold at least `need` bytes (growing them waits for
 // the stream: never inside a stream capture).
 bool backend_xscratch_reserve(Backend* be, size_t need) {
+    if (need > be->xscratch_bytes && be->xg.ok) {
+        set_error("a GEMV launch needs %zu bytes of scratch, more than the exchange region's %zu-byte slots "
+                  "(XDNA_B200_XSLOT_MB)",
+                  need, be->xscratch_bytes);
+        return false;
+    }
     if (need > be->xscratch_bytes) {
         if (cudaStreamSynchronize(be->stream) != cudaSuccess) return false;
         const size_t cap = std::max<size_t>(need, 1u << 20);
@@ -365,7 +373,10 @@ void* backend_xscratch(Backend* be, int64_t N, int64_t K) {
 bool nccl_wait(ncclComm_t comm, ncclResult_t r, const char* what);
 
 // Exchange regions: [flags: one uint32 per source rank, then this rank's
-// epoch counter at byte 128; 256 B][half 0][half 1].
+// epoch counter at byte 128; 256 B][half 0][half 1][x-scratch slot 0][slot 1].
+// The slots are the backend's GEMV scratch: a sharded launch writes the next
+// launch's x into the same slot of every rank (XDNA_B200_XSLOT_MB each,
+// default 8).
 constexpr size_t kXchgFlagBytes = 256;
 constexpr size_t kXchgEpochOffset = 128;
 
@@ -375,6 +386,7 @@ void release_exchange(Backend* be) {
         if (x.peer[p] && x.peer[p] != x.local) cudaIpcCloseMemHandle(x.peer[p]);
     if (x.local) cudaFree(x.local);
     if (x.err) cudaFree(x.err);
+    if (x.base_table) cudaFree(x.base_table);
     x = Backend::Exchange{};
 }
 
@@ -387,7 +399,8 @@ bool setup_exchange(Backend* be) {
     const char* mb = getenv("XDNA_B200_XCHG_MB");
     const size_t half_bytes = (mb ? static_cast<size_t>(atol(mb)) : 16) << 20;
     x.cap_floats = half_bytes / sizeof(float);
-    const size_t bytes = kXchgFlagBytes + 2 * half_bytes;
+    x.slot_bytes = env_size("XDNA_B200_XSLOT_MB", 8) << 20;
+    const size_t bytes = kXchgFlagBytes + 2 * half_bytes + 2 * x.slot_bytes;
     bool ok = cuda_ok(cudaMalloc(&x.local, bytes), "exchange alloc") &&
               cuda_ok(cudaMemset(x.local, 0, bytes), "exchange clear") &&
               cuda_ok(cudaMalloc(&x.err, sizeof(int)), "exchange error word") &&
@@ -434,6 +447,21 @@ bool setup_exchange(Backend* be) {
         return false;
     }
     x.epoch = reinterpret_cast<uint32_t*>(x.local + kXchgEpochOffset);  // zero: cleared with the region
+    std::vector<float*> bases(be->world);
+    for (int p = 0; p < be->world; ++p) bases[p] = reinterpret_cast<float*>(x.peer[p] + kXchgFlagBytes);
+    if (!cuda_ok(cudaMalloc(&x.base_table, sizeof(float*) * be->world), "exchange base table") ||
+        !cuda_ok(cudaMemcpy(x.base_table, bases.data(), sizeof(float*) * be->world, cudaMemcpyHostToDevice),
+                 "exchange base table upload")) {
+        release_exchange(be);
+        return false;
+    }
+    // the GEMV scratch slots move into the exchange region (zeroed with it)
+    for (int s = 0; s < 2; ++s) {
+        if (be->xscratch[s]) cudaFree(be->xscratch[s]);
+        be->xscratch[s] = x.local + kXchgFlagBytes + 2 * half_bytes + s * x.slot_bytes;
+    }
+    be->xscratch_bytes = x.slot_bytes;
+    ++be->scratch_gen;
     x.ok = true;
     return true;
 }
@@ -769,6 +797,11 @@ struct MmaPlan {
     void* scratch = nullptr;
     const MmaFeed* feed = nullptr;
     bool x_ready = false;
+    // sharded chain: the feed goes to every rank (no gather kernel after this
+    // launch), and this launch assembles the previous launch's outputs
+    bool feed_peers = false;
+    int nprev = 0;
+    GatherSeg prev[MMA_MAX_SEGMENTS];
 };
 
 bool run_node(Backend* be, ggml_tensor_xdna* node, const MmaPlan* plan = nullptr) {
@@ -1023,6 +1056,7 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n, const MmaPlan* plan 
             pe.peer_data[p] = reinterpret_cast<float*>(xg.peer[p] + kXchgFlagBytes);
             pe.peer_flags[p] = reinterpret_cast<uint32_t*>(xg.peer[p]);
         }
+        pe.err = xg.err;
         GatherSeg gs[MMA_MAX_SEGMENTS];
         int64_t off = 0;
         for (size_t k = 0; k < n; ++k) {
@@ -1030,11 +1064,20 @@ bool run_fused(Backend* be, const FusableNode* f, size_t n, const MmaPlan* plan 
             gs[k] = GatherSeg{f[k].y_full, f[k].seg.N, off};
             off += f[k].n_out;
         }
-        // a planned feed is done by the gather, which holds the full output
-        return cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream,
-                                             true, &pe, nullptr, plan && plan->x_ready),
-                       "sharded gemv launch") &&
-               cuda_ok(xchg_gather_launch(reinterpret_cast<const float*>(xg.local + kXchgFlagBytes),
+        ShardChain sc;
+        sc.peer_base = xg.base_table;
+        sc.feed_peers = plan && plan->feed_peers;
+        sc.nprev = plan ? plan->nprev : 0;
+        sc.prev = plan ? plan->prev : nullptr;
+        if (!cuda_ok(gemv_mma_multi_launch(f[0].type, segs, static_cast<int>(n), f[0].x, f[0].K, scratch, be->stream,
+                                           true, &pe, sc.feed_peers ? plan->feed : nullptr, plan && plan->x_ready,
+                                           false, &sc),
+                     "sharded gemv launch"))
+            return false;
+        // the next sharded launch assembles these outputs itself; otherwise a
+        // gather (which also prepares a planned feed from the full output)
+        if (sc.feed_peers) return true;
+        return cuda_ok(xchg_gather_launch(reinterpret_cast<const float*>(xg.local + kXchgFlagBytes),
                                           static_cast<int64_t>(xg.cap_floats),
                                           reinterpret_cast<const uint32_t*>(xg.local), xg.epoch, be->world, be->rank,
                                           gs, static_cast<int>(n), xg.err, be->stream, plan ? plan->feed : nullptr),
@@ -1213,8 +1256,9 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         be->dev_arena.release();
         be->host_arena.release();
         be->wt_arena.release();
-        for (void* p : be->xscratch)
-            if (p) cudaFree(p);
+        if (!be->xg.ok)
+            for (void* p : be->xscratch)
+                if (p) cudaFree(p);
         release_exchange(be);
         drop_graph(be);
         if (be->comm) nccl_api().CommDestroy(be->comm);
@@ -1314,6 +1358,18 @@ static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
                 r.feed.bl = mma_blk16(q.f[0].type) ? 16 : 32;
                 r.plan.feed = &r.feed;
                 q.plan.x_ready = true;
+                // both sharded over the exchange: this launch's rows of the
+                // next x go to every rank, and the next launch (after waiting
+                // for the peers) completes this launch's outputs
+                if (r.f[0].sharded && q.f[0].sharded && r.f[j].seg.N % 32 == 0) {
+                    r.plan.feed_peers = true;
+                    q.plan.nprev = static_cast<int>(nseg);
+                    int64_t off = 0;
+                    for (size_t s2 = 0; s2 < nseg; ++s2) {
+                        q.plan.prev[s2] = GatherSeg{r.f[s2].y_full, r.f[s2].seg.N, off};
+                        off += r.f[s2].n_out;
+                    }
+                }
                 break;
             }
     }

@@ -77,10 +77,28 @@ struct PeerExchange {
     int64_t half_floats;               // floats per data half
     uint32_t* epoch;                   // this rank's epoch counter (device memory)
     int64_t xo[4];                     // segment s's first float in the exchange buffer
+    int* err;                          // set when a bounded wait for the peers runs out
+};
+// A chain of row-sharded launches without gather kernels between them: a
+// launch whose output segment is the next launch's x (MmaFeed) prepares its
+// own rows' part of that x into its local scratch and, over NVLink, into the
+// same scratch slot of every peer (the slots sit at one offset of every
+// rank's exchange region, whose base addresses `peer_base` lists in device
+// memory).  The next launch then waits (bounded) until every peer's flag
+// shows the previous epoch, and copies the previous launch's peer rows
+// (segments `prev`, from this GPU's exchange data of the previous epoch) into
+// their full outputs before it computes.
+struct GatherSeg;
+struct ShardChain {
+    bool feed_peers = false;
+    const float* const* peer_base = nullptr;  // [world]: each rank's exchange data half 0
+    int nprev = 0;
+    const GatherSeg* prev = nullptr;
 };
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg = nullptr,
-                                  const MmaFeed* feed = nullptr, bool x_ready = false, bool classic = false);
+                                  const MmaFeed* feed = nullptr, bool x_ready = false, bool classic = false,
+                                  const ShardChain* chain = nullptr);
 // Copy the peers' rows of each segment from this GPU's exchange buffer
 // (xdata: half 0) into the full outputs once every peer's flag reaches the
 // launch's epoch, read from *epoch after the GEMV has stored it (a bounded

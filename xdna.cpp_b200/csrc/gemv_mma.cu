@@ -50,6 +50,9 @@ __device__ __forceinline__ uint64_t global_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Bounded waits on the peers' flags: 1 s of %globaltimer.
+constexpr uint64_t kGatherWaitNs = 1000000000ull;
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
@@ -137,9 +140,24 @@ __device__ __forceinline__ uint32_t digit_word(uint32_t v0, uint32_t v1, uint32_
 // BL = values per x block (B column): 32, or 16 for the formats with
 // 16-value sub-blocks (chunks 0-3 then cover blocks 0-7, chunks 4-7 blocks
 // 8-15 of the group).
+// Peer copies of a prepared x (row-sharded chains): the same bytes also go to
+// every other rank's scratch slot, at the same offset from that rank's
+// exchange base (pb[p]) as from this rank's (pb[rank]).
+struct PeerDest {
+    const float* const* pb;  // nullptr: none
+    int world, rank;
+};
+template <typename T>
+__device__ __forceinline__ T* at_peer(const PeerDest& d, int p, T* local) {
+    const char* mine = reinterpret_cast<const char*>(__ldg(reinterpret_cast<const unsigned long long*>(d.pb) + d.rank));
+    const char* theirs = reinterpret_cast<const char*>(__ldg(reinterpret_cast<const unsigned long long*>(d.pb) + p));
+    return reinterpret_cast<T*>(const_cast<char*>(theirs) + (reinterpret_cast<const char*>(local) - mine));
+}
+
 template <int BL>
 __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t* __restrict__ frags,
-                                         float* __restrict__ scale, float* __restrict__ xsum) {
+                                         float* __restrict__ scale, float* __restrict__ xsum,
+                                         const PeerDest pd = PeerDest{nullptr, 0, 0}) {
     const int64_t b = (w32 * 32 + lane) / BL;  // this lane's block
     // a block holding an infinity or a NaN gets a NaN scale and sum, so every
     // output it reaches is NaN, as in an F32 dot product (the fixed-point
@@ -176,17 +194,29 @@ __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t
         const int blk = jb & 7;                                          // B column
         const int c = (BL == 32 ? 0 : 4 * (jb >> 3)) + (lane % BL) / 4;  // chunk
         uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
-        if (blk < 4) {
-            slot[0] = make_uint4(D0, 0u, D1, 0u);
-            slot[1] = make_uint4(D2, 0u, 0u, 0u);
-        } else {
-            slot[0] = make_uint4(0u, D0, 0u, D1);
-            slot[1] = make_uint4(0u, D2, 0u, 0u);
-        }
+        const uint4 s0 = blk < 4 ? make_uint4(D0, 0u, D1, 0u) : make_uint4(0u, D0, 0u, D1);
+        const uint4 s1 = blk < 4 ? make_uint4(D2, 0u, 0u, 0u) : make_uint4(0u, D2, 0u, 0u);
+        slot[0] = s0;
+        slot[1] = s1;
+        if (pd.pb)
+            for (int p = 0; p < pd.world; ++p)
+                if (p != pd.rank) {
+                    uint4* ps = at_peer(pd, p, slot);
+                    ps[0] = s0;
+                    ps[1] = s1;
+                }
     }
     if (lane % BL == 0) {
-        scale[b] = bad ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
-        xsum[b] = bad ? __int_as_float(0x7fc00000) : s;
+        const float sv = bad ? __int_as_float(0x7fc00000) : ldexpf(1.0f, e);
+        const float xv = bad ? __int_as_float(0x7fc00000) : s;
+        scale[b] = sv;
+        xsum[b] = xv;
+        if (pd.pb)
+            for (int p = 0; p < pd.world; ++p)
+                if (p != pd.rank) {
+                    *at_peer(pd, p, scale + b) = sv;
+                    *at_peer(pd, p, xsum + b) = xv;
+                }
     }
 }
 
@@ -244,6 +274,14 @@ struct GemvArgs {
     int64_t f_ncount;
     uint32_t* f_zeros;
     int* err;           // set when a bounded wait (shared-memory ring) runs out
+    // row-sharded chain (ShardChain): the feed also goes to the peers; this
+    // launch waits for the peers' previous epoch and assembles the previous
+    // launch's outputs (prev) before computing
+    const float* const* f_pbase;
+    int64_t f_ch0;      // the fed output's first 32-value chunk in the full vector (this rank's rows)
+    int wait_peers;
+    int nprev;
+    GatherSeg prev[kMaxSegs];
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -932,7 +970,7 @@ __host__ __device__ constexpr size_t ring_offset(int cta_tiles) {
 // Called once per emitted tile and kept out of line, so that it adds nothing
 // to the register budget of the streaming loop.
 __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum, int* chunk, const float* y, int lt,
-                                      int bl, int lane) {
+                                      int bl, int lane, int64_t ch0, const PeerDest pd) {
     const int ch = lt >> 1;  // lt: the tile's index within the feeding output
     __threadfence();
     __syncwarp();
@@ -943,9 +981,9 @@ __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum
     __threadfence();
     const float v = __ldcg(y + int64_t(ch) * 32 + lane);
     if (bl == 16)
-        prep_x32<16>(v, ch, lane, frags, scale, xsum);
+        prep_x32<16>(v, ch0 + ch, lane, frags, scale, xsum, pd);
     else
-        prep_x32<32>(v, ch, lane, frags, scale, xsum);
+        prep_x32<32>(v, ch0 + ch, lane, frags, scale, xsum, pd);
 }
 
 // kTiles: tile mode (a compile-time choice, so the unit-mode kernel carries
@@ -1037,6 +1075,46 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         const int64_t gt = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
         for (int64_t i = gt; i < a.f_ncount; i += int64_t(gridDim.x) * blockDim.x) a.f_count[i] = 0;
         if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
+    }
+    if (a.wait_peers) {
+        // Sharded chain: part of this launch's x was prepared by the peers
+        // (their rows of the previous launch's output).  Their flags of the
+        // previous epoch cover those stores; the wait is bounded and a
+        // time-out is reported through the exchange's error word.
+        __shared__ int s_peers_ok;
+        if (threadIdx.x == 0) {
+            int ok = 1;
+            const uint32_t* fl = a.x.peer_flags[a.x.rank];
+            const uint64_t w0 = global_ns();
+            for (int p = 0; p < a.x.world && ok; ++p) {
+                if (p == a.x.rank) continue;
+                while (static_cast<int32_t>(ld_acquire_sys(fl + p) - (xe - 1u)) < 0) {
+                    if (global_ns() - w0 > kGatherWaitNs) {
+                        ok = 0;
+                        atomicExch(a.x.err, 1);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            s_peers_ok = ok;
+        }
+        __syncthreads();
+        if (s_peers_ok) {
+            // the previous launch's peer rows -> its full outputs (this GPU's
+            // exchange data of the previous epoch)
+            const float* xd = a.x.peer_data[a.x.rank] + (((xe - 1u) & 1u) ? a.x.half_floats : 0);
+            const int64_t gt = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+            const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+            for (int sg = 0; sg < a.nprev; ++sg) {
+                const GatherSeg ps = a.prev[sg];
+                const int64_t n_peers = ps.n_local * a.x.world;
+                for (int64_t i = gt; i < n_peers; i += stride) {
+                    if (i / ps.n_local == a.x.rank) continue;  // own rows: written by the previous launch
+                    ps.y_full[i] = __ldcg(xd + ps.xo + i);
+                }
+            }
+        }
     }
 
     const bool supplier = g == t || g == t + 4;
@@ -1158,7 +1236,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             }
         }
         if (emitted && a.f_bl != 0 && tile >= a.f_t0 && tile < a.f_t1)
-            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl, lane);
+            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(tile - a.f_t0), a.f_bl, lane, a.f_ch0,
+                      PeerDest{a.f_pbase, a.x.world, a.x.rank});
         u = tbeg + gend;
     }
     if constexpr (kRing) {
@@ -1487,8 +1566,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
             }
         }
         if (emitted && a.f_bl != 0 && my_tile >= a.f_t0 && my_tile < a.f_t1)
-            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(my_tile - a.f_t0), a.f_bl,
-                      lane);
+            feed_next(a.f_frags, a.f_scale, a.f_xsum, a.f_chunk, a.f_y, static_cast<int>(my_tile - a.f_t0), a.f_bl, lane, a.f_ch0,
+                      PeerDest{a.f_pbase, a.x.world, a.x.rank});
     }
     if (!ok) {
         if (lane == 0) atomicExch(b.err, 1);
@@ -1524,7 +1603,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
 // sees both halves of every output.  The flag wait is bounded (1 s of
 // %globaltimer); on time-out *err is set and nothing is copied, so the host
 // reports an error instead of the GPU hanging.
-constexpr uint64_t kGatherWaitNs = 1000000000ull;  // 1 s of %globaltimer
 struct GatherArgs {
     GatherSeg seg[kMaxSegs];
     int nseg;
@@ -2019,7 +2097,7 @@ cudaError_t gemv_mma_launch(int type, const void* W, const float* x, float* y, i
 
 cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, const float* x, int64_t K,
                                   void* scratch, cudaStream_t stream, bool pdl, const PeerExchange* xchg,
-                                  const MmaFeed* feed, bool x_ready, bool classic) {
+                                  const MmaFeed* feed, bool x_ready, bool classic, const ShardChain* chain) {
     if (layout_kind(type, MMA_TILE_ROWS, 256) != 1 ||
         nseg < 1 || nseg > kMaxSegs)
         return cudaErrorInvalidValue;
@@ -2051,12 +2129,24 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     a.partial = reinterpret_cast<float*>(base + L.partial);
     a.ngroups = ngroups;
     a.units = ntiles * ngroups;
+    if (chain && (!xchg || chain->nprev < 0 || chain->nprev > kMaxSegs || (chain->nprev > 0 && !chain->prev) ||
+                  (chain->feed_peers && (!feed || !chain->peer_base))))
+        return cudaErrorInvalidValue;
+    const bool feed_peers = chain && chain->feed_peers;
+    if (chain) {
+        a.wait_peers = chain->nprev > 0 ? 1 : 0;
+        a.nprev = chain->nprev;
+        for (int s = 0; s < chain->nprev; ++s) a.prev[s] = chain->prev[s];
+    }
     if (feed) {
         // the next launch's x is segment feed->seg in full: K_next = its N
-        if (xchg || !feed->next_scratch || feed->seg < 0 || feed->seg >= nseg || segs[feed->seg].N % 256 != 0 ||
-            (feed->bl != 16 && feed->bl != 32) || feed->next_rows <= 0 || feed->next_rows % MMA_TILE_ROWS != 0)
+        // (times the ranks when this rank's rows go to every peer as well)
+        const int64_t nf = segs[feed->seg].N, kn = feed_peers ? nf * xchg->world : nf;
+        if ((xchg && !feed_peers) || !feed->next_scratch || feed->seg < 0 || feed->seg >= nseg || kn % 256 != 0 ||
+            (feed_peers && nf % 32 != 0) || (feed->bl != 16 && feed->bl != 32) || feed->next_rows <= 0 ||
+            feed->next_rows % MMA_TILE_ROWS != 0)
             return cudaErrorInvalidValue;
-        const ScratchLayout Ln = scratch_layout(MMA_TILE_ROWS, segs[feed->seg].N);  // x offsets depend on K only
+        const ScratchLayout Ln = scratch_layout(MMA_TILE_ROWS, kn);  // x offsets depend on K only
         uint8_t* nb = static_cast<uint8_t*>(feed->next_scratch);
         a.f_frags = nb + Ln.frags;
         a.f_scale = reinterpret_cast<float*>(nb + Ln.scale);
@@ -2067,7 +2157,11 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         a.f_t1 = a.tile_end[feed->seg];
         a.f_bl = feed->bl;
         const int64_t nt = feed->next_rows / MMA_TILE_ROWS;
-        const ScratchLayout Lf = scratch_layout(feed->next_rows, segs[feed->seg].N);
+        const ScratchLayout Lf = scratch_layout(feed->next_rows, kn);
+        if (feed_peers) {
+            a.f_pbase = chain->peer_base;
+            a.f_ch0 = xchg->rank * nf / 32;
+        }
         a.f_count = reinterpret_cast<int*>(nb + Lf.count);
         a.f_ncount = counter_ints(nt);
         a.f_zeros = reinterpret_cast<uint32_t*>(nb + Lf.zeros);
@@ -2123,7 +2217,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         if (e != cudaSuccess) return e;
     }
 
-    const int choice = classic ? 0 : gemv_kernel_choice();
+    const int choice = classic ? 0 : (xchg && gemv_kernel_choice() != 3 ? 0 : gemv_kernel_choice());
     if (choice == 1 || choice == 2) {
         bool used = false;
         const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, stream, &used);
