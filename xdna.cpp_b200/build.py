@@ -3,7 +3,8 @@
     python build.py [--clean]
 
 Outputs land next to this file: ``libggml-b200.so`` and ``_build/`` (object
-files and the generated IQ table header).  The shared object links the CUDA
+files and the generated IQ table header); with XDNA_LLAMA_CPP_DIR set to a
+llama.cpp / ggml tree, also the ggml plugin ``libggml-b200-ggml.so``.  The shared object links the CUDA
 runtime statically so it can be dlopen'ed by a ggml host or ctypes without
 any Python or torch runtime.
 """
@@ -54,7 +55,36 @@ def build(verbose: bool = False) -> str:
     if _stale(LIB, objs):
         subprocess.run([NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart_static", "-lrt", "-ldl", "-lpthread"],
                        check=True)
+    build_ggml_adapter()
     return LIB
+
+
+GGML_ADAPTER = os.path.join(HERE, "libggml-b200-ggml.so")
+
+
+def build_ggml_adapter() -> str | None:
+    """The ggml plugin (ggml/ggml-b200-adapter.cpp -> libggml-b200-ggml.so,
+    the library GGML_BACKEND_PATH names), built only when XDNA_LLAMA_CPP_DIR
+    points at a llama.cpp / ggml source tree: its ggml/include and ggml/src
+    supply ggml.h, ggml-backend.h and ggml-backend-impl.h.  ggml's own symbols
+    resolve at load time from the ggml host process; libggml-b200.so is found
+    next to the adapter."""
+    tree = os.environ.get("XDNA_LLAMA_CPP_DIR")
+    if not tree:
+        return None
+    inc = [os.path.join(tree, "ggml", "include"), os.path.join(tree, "ggml", "src")]
+    if not os.path.exists(os.path.join(inc[0], "ggml-backend.h")) or not os.path.exists(
+            os.path.join(inc[1], "ggml-backend-impl.h")):
+        raise SystemExit(f"XDNA_LLAMA_CPP_DIR={tree}: ggml/include/ggml-backend.h or ggml/src/ggml-backend-impl.h "
+                         "not found")
+    src = os.path.join(HERE, "ggml", "ggml-b200-adapter.cpp")
+    hdrs = [os.path.join(HERE, "..", "include", h) for h in ("ggml-b200.h", "ggml-b200-convert.h")]
+    if _stale(GGML_ADAPTER, [src, LIB] + hdrs):
+        cxx = os.environ.get("CXX", "g++")
+        subprocess.run([cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra"]
+                       + sum((["-I", d] for d in inc + [os.path.join(HERE, "..", "include")]), [])
+                       + [src, "-o", GGML_ADAPTER, "-L", HERE, "-lggml-b200", "-Wl,-rpath,$ORIGIN"], check=True)
+    return GGML_ADAPTER
 
 
 if __name__ == "__main__":
