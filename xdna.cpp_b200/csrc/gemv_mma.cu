@@ -123,7 +123,7 @@ constexpr int kWarps = 24;
 constexpr int kGemvThreads = kWarps * 32;
 constexpr int kCtasPerSm = 1;
 constexpr int kMaxCtas = 512;        // bounds the partial-slot area
-constexpr int kPrefetch = 4;         // groups ahead per warp (bulk L2 prefetch)
+constexpr int kPrefetch = 2;         // groups ahead per warp (bulk L2 prefetch; 2 measured ahead of 4 and 8)
 constexpr int kSlotBytes = 32;
 constexpr int kChunkFragBytes = 8 * kSlotBytes;       // 8 blocks
 constexpr int kGroupFragBytes = 8 * kChunkFragBytes;  // 8 chunks: 2 KiB per 256 values
@@ -316,8 +316,17 @@ __device__ __forceinline__ void emit(const GemvArgs& a, float* ty, int tile, int
     }
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// The peers' flags of a finished sharded launch, raised by the CTA that
+// counted in last: one system-scope release fence (cumulative over every
+// CTA's stores, which it observed through the completion counter) followed
+// by plain system-scope stores, so the flags of all peers share one fence.
+__device__ __forceinline__ void raise_peer_flags(const PeerExchange& x, uint32_t e) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int p = 0; p < x.world; ++p)
+        if (p != x.rank) st_relaxed_sys(x.peer_flags[p] + x.rank, e);
 }
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
@@ -1259,14 +1268,13 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         // in then fences at system scope, which, being cumulative over what it
         // observed through the counter, orders all CTAs' stores before this
         // rank's flag in each peer's flag array.  (A system-scope fence in
-        // every CTA cost about 8 us per launch.)
+        // every CTA cost about 8 us per launch; a fence per peer flag, on top
+        // of an explicit one, about 1.7 us more at N = 2.)
         __syncthreads();
         if (threadIdx.x == 0) {
             __threadfence();
             if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
-                __threadfence_system();
-                for (int p = 0; p < a.x.world; ++p)
-                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, xe);
+                raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;  // every CTA has read e - 1 (before counting in)
             }
         }
@@ -1587,9 +1595,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
             }
             __threadfence();
             if (atomicAdd(a.done, 1) == G - 1) {
-                __threadfence_system();
-                for (int p = 0; p < a.x.world; ++p)
-                    if (p != a.x.rank) st_release_sys(a.x.peer_flags[p] + a.x.rank, xe);
+                raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;
             }
         }
@@ -1839,6 +1845,10 @@ size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).to
 // against 3532 ring, 2859 bulk and 3424 bulkx; the 70B decode step 10.39 ms
 // against 11.52 ring and 15.34 bulkx), so the others are opt-in.  Read once
 // per process.
+static bool gemv_kernel_choice_set() {
+    static const bool set = getenv("XDNA_B200_GEMV") != nullptr;
+    return set;
+}
 static int gemv_kernel_choice() {
     static const int choice = [] {
         const char* v = getenv("XDNA_B200_GEMV");
@@ -2217,7 +2227,11 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         if (e != cudaSuccess) return e;
     }
 
-    const int choice = classic ? 0 : (xchg && gemv_kernel_choice() != 3 ? 0 : gemv_kernel_choice());
+    // sharded launches take the ring variant unless a choice is set: their
+    // weights stream in while the launch waits for the previous one and the
+    // peers (N = 2 decode step: 9.16 ms against 10.15 with streaming loads)
+    const int choice = classic ? 0 : (xchg ? (gemv_kernel_choice_set() ? gemv_kernel_choice() : 3) : gemv_kernel_choice());
+    if (xchg && (choice == 1 || choice == 2)) return cudaErrorInvalidValue;  // the bulk kernel has no exchange
     if (choice == 1 || choice == 2) {
         bool used = false;
         const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, stream, &used);
