@@ -328,6 +328,23 @@ __device__ __forceinline__ void raise_peer_flags(const PeerExchange& x, uint32_t
     for (int p = 0; p < x.world; ++p)
         if (p != x.rank) st_relaxed_sys(x.peer_flags[p] + x.rank, e);
 }
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+// A warp counts in at *p once: every lane's earlier stores are released
+// with lane 0's atomic (the warp barrier orders them before it), and every
+// lane's later loads are ordered after it.  Returns the old count to all
+// lanes.  One acquire-release atomic in place of a fence on each side.
+__device__ __forceinline__ int warp_count_in(int* p) {
+    __syncwarp();
+    int prev = 0;
+    if ((threadIdx.x & 31) == 0) prev = atom_add_acq_rel_gpu(p, 1);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    __syncwarp();
+    return prev;
+}
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -981,13 +998,7 @@ __host__ __device__ constexpr size_t ring_offset(int cta_tiles) {
 __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum, int* chunk, const float* y, int lt,
                                       int bl, int lane, int64_t ch0, const PeerDest pd) {
     const int ch = lt >> 1;  // lt: the tile's index within the feeding output
-    __threadfence();
-    __syncwarp();
-    int prev = 0;
-    if (lane == 0) prev = atomicAdd(chunk + ch, 1);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev == 0) return;
-    __threadfence();
+    if (warp_count_in(chunk + ch) == 0) return;
     const float v = __ldcg(y + int64_t(ch) * 32 + lane);
     if (bl == 16)
         prep_x32<16>(v, ch0 + ch, lane, frags, scale, xsum, pd);
@@ -1214,13 +1225,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     // level 2: the CTA's sum to global memory; the last CTA adds them in CTA order.
                     // A CTA shares at most two tiles with others: its first (slot 0) and last (slot 1).
                     if (lane < MMA_TILE_ROWS) a.partial[(cta * 2 + (tile == t0 ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
-                    __threadfence();
-                    __syncwarp();
-                    int gprev = 0;
-                    if (lane == 0) gprev = atomicAdd(a.count + tile, 1);
-                    gprev = __shfl_sync(0xffffffffu, gprev, 0);
+                    const int gprev = warp_count_in(a.count + tile);
                     if (gprev == cb - ca) {
-                        __threadfence();
                         // lane (row r, half h) adds CTAs ca + h, ca + h + 2, ..., eight loads in flight
                         const int h = lane >> 4;
                         // CTA ca's first tile (unit mode only: in tile mode no tile spans CTAs)
@@ -1272,8 +1278,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         // of an explicit one, about 1.7 us more at N = 2.)
         __syncthreads();
         if (threadIdx.x == 0) {
-            __threadfence();
-            if (atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
+            if (atom_add_acq_rel_gpu(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
                 raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;  // every CTA has read e - 1 (before counting in)
             }
@@ -1556,13 +1561,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
             const int ca = cta_of_unit(ts, U, G), cb = cta_of_unit(ts + ng - 1, U, G);
             if (lane < MMA_TILE_ROWS)
                 a.partial[(cta * 2 + (my_tile == first_tile ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
-            __threadfence();
-            __syncwarp();
-            int prev = 0;
-            if (lane == 0) prev = atomicAdd(a.count + my_tile, 1);
-            prev = __shfl_sync(0xffffffffu, prev, 0);
+            const int prev = warp_count_in(a.count + my_tile);
             if (prev == cb - ca) {
-                __threadfence();
                 float sum = 0.f;
                 if (lane < MMA_TILE_ROWS)
                     for (int c2 = ca; c2 <= cb; ++c2) {
@@ -1593,8 +1593,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
                 atomicExch(b.err, 1);
                 return;
             }
-            __threadfence();
-            if (atomicAdd(a.done, 1) == G - 1) {
+            if (atom_add_acq_rel_gpu(a.done, 1) == G - 1) {
                 raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;
             }
@@ -1845,10 +1844,6 @@ size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).to
 // against 3532 ring, 2859 bulk and 3424 bulkx; the 70B decode step 10.39 ms
 // against 11.52 ring and 15.34 bulkx), so the others are opt-in.  Read once
 // per process.
-static bool gemv_kernel_choice_set() {
-    static const bool set = getenv("XDNA_B200_GEMV") != nullptr;
-    return set;
-}
 static int gemv_kernel_choice() {
     static const int choice = [] {
         const char* v = getenv("XDNA_B200_GEMV");
@@ -2227,10 +2222,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         if (e != cudaSuccess) return e;
     }
 
-    // sharded launches take the ring variant unless a choice is set: their
-    // weights stream in while the launch waits for the previous one and the
-    // peers (N = 2 decode step: 9.16 ms against 10.15 with streaming loads)
-    const int choice = classic ? 0 : (xchg ? (gemv_kernel_choice_set() ? gemv_kernel_choice() : 3) : gemv_kernel_choice());
+    const int choice = classic ? 0 : gemv_kernel_choice();
     if (xchg && (choice == 1 || choice == 2)) return cudaErrorInvalidValue;  // the bulk kernel has no exchange
     if (choice == 1 || choice == 2) {
         bool used = false;
