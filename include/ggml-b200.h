@@ -191,6 +191,12 @@ int b200_gemv_multi(int type, const void *const *w_packed, float *const *y, cons
  * stream of the device: calls whose executions overlap in time race. */
 int b200_gemv_noalloc(int type, const void *w_packed, const float *x, float *y, int64_t n, int64_t k,
                       void *stream);
+/* Status of the GEMV kernels' bounded waits on the current CUDA device:
+ * *status = 1 if a wait inside a shared-memory GEMV variant (XDNA_B200_GEMV =
+ * ring / bulk / bulkx) ran out since the last call, else 0; the word is
+ * cleared.  Returns 0, or a negative code on a CUDA error.  No reference
+ * counterpart (its engine has no device waits). */
+int b200_gemv_error(int *status);
 /* GGUF rows -> device layout (MMA tiles or stripe tiles, as b200_gemv
  * describes; out of place), the GPU replacement of the
  * reference's Q4Prepacker::pack (src/xdna-q4-prepack.cpp:39-114). */

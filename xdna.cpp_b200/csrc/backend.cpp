@@ -1813,6 +1813,14 @@ int b200_gemv_noalloc(int type, const void* w_packed, const float* x, float* y, 
                      "b200_gemv_noalloc");
 }
 
+int b200_gemv_error(int* status) {
+    if (!status) {
+        set_error("b200_gemv_error: null status pointer");
+        return -1;
+    }
+    return launch_rc(gemv_error_status(status), "b200_gemv_error");
+}
+
 int b200_repack(int type, const void* raw, void* packed, int64_t n, int64_t k, void* stream) {
     return launch_rc(repack_launch(type, raw, packed, n, k, 0, n, static_cast<cudaStream_t>(stream)), "b200_repack");
 }

@@ -128,6 +128,7 @@ def lib() -> C.CDLL:
         "b200_gemv_noalloc": (C.c_int, [C.c_int, vp, vp, vp, i64, i64, vp]),
         "b200_gemv_multi": (C.c_int, [C.c_int, C.POINTER(vp), C.POINTER(vp), C.POINTER(i64), C.c_int, vp, i64, vp,
                                       C.c_int]),
+        "b200_gemv_error": (C.c_int, [C.POINTER(C.c_int)]),
         "b200_repack": (C.c_int, [C.c_int, vp, vp, i64, i64, vp]),
         "b200_unpack": (C.c_int, [C.c_int, vp, vp, i64, i64, vp]),
         "b200_bf16_to_f32": (C.c_int, [vp, vp, i64, vp]),
