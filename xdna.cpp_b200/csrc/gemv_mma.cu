@@ -111,10 +111,8 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //   zeros   32 zero bytes: the B "slot" of the 24 lanes that supply nothing
 //   scale   2^e per 32-value block;  xsum  sum of the block's x
 //   count   one arrival counter per tile, the CTA completion counter and one
-//           per 32-value chunk of a feeding output; in the backend's and the
-//           launcher's slots a fixed region at the start of the slot, kept
-//           zero by each counter's last user (and also cleared by
-//           xprep_kernel, or by the previous launch when it prepared x)
+//           per 32-value chunk of a feeding output (cleared by xprep_kernel,
+//           or by the previous launch when it prepared x)
 //   partial kMaxCtas CTAs * 2 slots * 16 floats (level-2 CTA sums)
 // ---------------------------------------------------------------------------
 // One CTA of 24 warps per SM: warps of one CTA are scheduled as equals,
@@ -1328,7 +1326,6 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
             if (atom_add_acq_rel_gpu(a.done, 1) == static_cast<int>(gridDim.x) - 1) {
                 raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;  // every CTA has read e - 1 (before counting in)
-                *a.done = 0;      // every CTA counted in: clear for the slot's next launch
             }
         }
     }
@@ -1645,7 +1642,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
             if (atom_add_acq_rel_gpu(a.done, 1) == G - 1) {
                 raise_peer_flags(a.x, xe);
                 *a.x.epoch = xe;
-                *a.done = 0;
             }
         }
     }
@@ -1865,38 +1861,23 @@ static int sm_count() {
 // before when that one prepares x.
 static int64_t counter_ints(int64_t ntiles) { return ntiles + 1 + ntiles / 2 + 1; }
 
-// Counters sit first in every scratch slot the backend and the launcher hand
-// out, in a region of fixed size, so that whatever shape used a slot before,
-// the bytes a launch counts with were counters then too (left at zero by
-// their last user: tile and chunk counters clear themselves) and never x
-// data, whose offsets depend on K.  Up to 43,690 tiles (699,040 rows).
-constexpr int64_t kCounterInts = int64_t(1) << 16;
-
-static ScratchLayout layout_impl(int64_t N, int64_t K, bool fixed_counters) {
+// Scratch of one MMA GEMV launch (layout described above the kernels).
+ScratchLayout scratch_layout(int64_t N, int64_t K) {
     auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
     ScratchLayout L;
     const size_t ngroups = static_cast<size_t>(K / 256), nblk = static_cast<size_t>(K / 32);
     const size_t ntiles = static_cast<size_t>(N / MMA_TILE_ROWS);
-    const size_t counters = fixed_counters ? size_t(kCounterInts) : size_t(counter_ints(static_cast<int64_t>(ntiles)));
-    L.count = 0;
-    L.frags = fixed_counters ? up(counters * sizeof(int)) : 0;
+    L.frags = 0;
     L.zeros = up(L.frags + ngroups * kGroupFragBytes);
     L.scale = up(L.zeros + kSlotBytes);
     L.xsum = up(L.scale + 2 * nblk * sizeof(float));  // room for 16-value blocks
-    if (!fixed_counters) L.count = up(L.xsum + 2 * nblk * sizeof(float));
-    L.partial = fixed_counters ? up(L.xsum + 2 * nblk * sizeof(float)) : up(L.count + counters * sizeof(int));
+    L.count = up(L.xsum + 2 * nblk * sizeof(float));
+    L.partial = up(L.count + counter_ints(static_cast<int64_t>(ntiles)) * sizeof(int));
     L.total = up(L.partial + size_t(kMaxCtas) * 2 * MMA_TILE_ROWS * sizeof(float));
     return L;
 }
 
-// The layout of the backend's and the launcher's scratch slots.
-ScratchLayout scratch_layout(int64_t N, int64_t K) { return layout_impl(N, K, true); }
-
-// The compact layout of b200_gemv_noalloc's fixed array, whose launches
-// always clear their counters with the x-preparation kernel.
-static ScratchLayout scratch_layout_compact(int64_t N, int64_t K) { return layout_impl(N, K, false); }
-
-size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout_compact(N, K).total; }
+size_t xprep_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
 size_t gemv_scratch_bytes(int64_t N, int64_t K) { return scratch_layout(N, K).total; }
 
@@ -2191,9 +2172,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         a.tile_end[s] = ntiles;
     }
     a.nseg = nseg;
-    if (!classic && counter_ints(ntiles) > kCounterInts) return cudaErrorInvalidValue;  // beyond 699,040 rows
-    const ScratchLayout L = classic ? scratch_layout_compact(ntiles * MMA_TILE_ROWS, K)
-                                    : scratch_layout(ntiles * MMA_TILE_ROWS, K);
+    const ScratchLayout L = scratch_layout(ntiles * MMA_TILE_ROWS, K);
     uint8_t* base = static_cast<uint8_t*>(scratch);
     const int64_t ngroups = K / 256, nblk = K / 32;
     a.frags = base + L.frags;
