@@ -282,7 +282,6 @@ struct GemvArgs {
     int wait_peers;
     int nprev;
     GatherSeg prev[kMaxSegs];
-    const float* x_raw;  // self-prepared launches (kXS): the F32 x every CTA prepares into shared memory
 };
 
 // Matrix s of a (global) tile, and that matrix's first tile, weights and
@@ -436,7 +435,6 @@ struct LdGlobal {
     static __device__ __forceinline__ uint32_t h(const uint8_t* p) {
         return __ldg(reinterpret_cast<const unsigned short*>(p));
     }
-    static __device__ __forceinline__ float2 f2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
 };
 struct LdShared {
     static __device__ __forceinline__ uint4 q(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
@@ -444,7 +442,6 @@ struct LdShared {
     static __device__ __forceinline__ uint2 d(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
     static __device__ __forceinline__ uint32_t w(const uint8_t* p) { return *reinterpret_cast<const unsigned int*>(p); }
     static __device__ __forceinline__ uint32_t h(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
-    static __device__ __forceinline__ float2 f2(const float* p) { return *reinterpret_cast<const float2*>(p); }
 };
 
 // One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
@@ -491,8 +488,8 @@ __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* 
 #pragma unroll
         for (int k = 0; k < 4; ++k)
             T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
-        const float2 sc2 = X::f2(sc_ + 8 * st + 2 * t);
-        const float2 xs2 = X::f2(xs_ + 8 * st + 2 * t);
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
+        const float2 xs2 = reinterpret_cast<const float2*>(xs_ + 8 * st)[t];
         const uint32_t sg = (st ? scw.x >> 16 : scw.x), s8 = (st ? scw.y >> 16 : scw.y);
         const float kg0 = static_cast<float>(static_cast<int8_t>(sg & 0xFFu));
         const float kg1 = static_cast<float>(static_cast<int8_t>((sg >> 8) & 0xFFu));
@@ -552,8 +549,8 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
         float T[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) T[k] = static_cast<float>(C[2][k] * 65536 + C[1][k] * 256 + C[0][k]);
-        const float2 sc2 = X::f2(sc_ + 8 * st + 2 * t);
-        const float2 xs2 = X::f2(xs_ + 8 * st + 2 * t);
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
+        const float2 xs2 = reinterpret_cast<const float2*>(xs_ + 8 * st)[t];
         float k6[4];  // scales (i = 4 h + 2 st + b) minus 32
 #pragma unroll
         for (int hb = 0; hb < 4; ++hb) {
@@ -618,7 +615,7 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
 #pragma unroll
     for (int k = 0; k < 4; ++k)
         T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
-    const float2 sc2 = X::f2(sc_ + 2 * t);
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     // six-bit scales of sub-blocks 2t, 2t+1: low nibbles at bit 4 ib of
     // scales_l, high pairs at bit 2 ib of scales_h
     float k6[2][2];
@@ -689,7 +686,7 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
 #pragma unroll
     for (int k = 0; k < 4; ++k)
         T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
-    const float2 sc2 = X::f2(sc_ + 2 * t);
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     // scales of blocks 2t (low nibble) and 2t + 1 (high nibble) are byte t of the row's scales
     const uint32_t bg = (sg >> (8 * t)) & 0xFFu, b8 = (s8 >> (8 * t)) & 0xFFu;
     const float kg0 = static_cast<float>(1 + 2 * (bg & 0xFu)), kg1 = static_cast<float>(1 + 2 * (bg >> 4));
@@ -739,7 +736,7 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
 #pragma unroll
     for (int k = 0; k < 4; ++k)
         T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
-    const float2 sc2 = X::f2(sc_ + 2 * t);
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     // scales (top nibble of word p): p = 0 (g, 2t), 1 (g+8, 2t), 2 (g, 2t+1), 3 (g+8, 2t+1)
     const float kg0 = 0.5f * (0.5f + static_cast<float>(SS.x >> 28));
     const float k80 = 0.5f * (0.5f + static_cast<float>(SS.y >> 28));
@@ -801,7 +798,7 @@ __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t*
 #pragma unroll
         for (int k = 0; k < 4; ++k)
             T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
-        const float2 sc2 = X::f2(sc_ + 8 * st + 2 * t);
+        const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
         // nibble 4 st + 2 h + b: row g + 8 h, block 8 st + 2 t + b
         const uint32_t n = scw >> (16 * st);
         const float kg0 = 0.25f * (0.5f + static_cast<float>(n & 0xFu));
@@ -879,8 +876,8 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
         T[2] = static_cast<float>(C[2][2] * 4096 + C[1][2] * 16 + (C[0][2] >> 4));
         T[3] = static_cast<float>(C[2][3] * 4096 + C[1][3] * 16 + (C[0][3] >> 4));
     }
-    const float2 sc2 = X::f2(sc_ + 2 * t);
-    const float2 xs2 = X::f2(xs_ + 2 * t);
+    const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
+    const float2 xs2 = __ldg(reinterpret_cast<const float2*>(xs_) + t);
     const float s0 = sc2.x, s1 = sc2.y, x0 = xs2.x, x1 = xs2.y;
     if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
         // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four per word
@@ -989,13 +986,6 @@ template <int TYPE>
 constexpr size_t ring_bytes() {
     return size_t(kWarps) * kRingDepth<TYPE> * kUnitBytes<TYPE> + size_t(kWarps) * kRingDepth<TYPE> * 8;
 }
-// Self-prepared x (kXS): up to this many 256-value groups (K <= 16384),
-// whose fragments, scales and sums take at most 137 KiB of shared memory.
-constexpr int kXsMaxGroups = 64;
-template <int TYPE>
-constexpr size_t xs_bytes(int64_t ngroups) {
-    return size_t(ngroups) * kGroupFragBytes + 2 * size_t(ngroups) * kXBlocks<TYPE> * sizeof(float) + kSlotBytes;
-}
 __host__ __device__ constexpr size_t ring_offset(int cta_tiles) {
     return (size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(cta_tiles) * sizeof(int) + 127) & ~size_t(127);
 }
@@ -1009,7 +999,6 @@ __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum
                                       int bl, int lane, int64_t ch0, const PeerDest pd) {
     const int ch = lt >> 1;  // lt: the tile's index within the feeding output
     if (warp_count_in(chunk + ch) == 0) return;
-    if (lane == 0) chunk[ch] = 0;  // both tiles are in: the counter is clear for the slot's next launch
     const float v = __ldcg(y + int64_t(ch) * 32 + lane);
     if (bl == 16)
         prep_x32<16>(v, ch0 + ch, lane, frags, scale, xsum, pd);
@@ -1024,12 +1013,7 @@ __device__ __noinline__ void feed_next(uint8_t* frags, float* scale, float* xsum
 // slot) kRingDepth units ahead, the first ones before the programmatic-launch
 // wait, and the warp reads each unit from shared memory once its barrier
 // completes.  Everything else (split, combine, epilogue) is the same.
-// kXS: x arrives as F32 (a.x_raw) and every CTA prepares all of it (digits,
-// scales, sums) into its own shared memory after the dependency wait, instead
-// of reading fragments an x-preparation kernel wrote: no such kernel and no
-// extra programmatic-launch hop ahead of a launch whose x no earlier launch
-// prepared.  For K up to kXsMaxGroups groups.
-template <int TYPE, bool kTiles, bool kRing = false, bool kXS = false>
+template <int TYPE, bool kTiles, bool kRing = false>
 __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(const GemvArgs a) {
     // unit, tile and group counts fit in 32 bits (the launcher checks)
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -1153,36 +1137,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         }
     }
 
-    const uint8_t* xfrags = a.frags;
-    const uint8_t* xzeros = a.zeros;
-    const float* xscale = a.scale;
-    const float* xsum = a.xsum;
-    if constexpr (kXS) {
-        // this CTA's copy of the prepared x, after the rings (none here) at the
-        // offset the launcher sized: fragments, scales, sums, zero slot
-        uint8_t* xb = reinterpret_cast<uint8_t*>(s_part) + ring_offset(a.cta_tiles);
-        float* sc = reinterpret_cast<float*>(xb + size_t(ng) * kGroupFragBytes);
-        float* sm = sc + ng * kXBlocks<TYPE>;
-        uint32_t* zs = reinterpret_cast<uint32_t*>(sm + ng * kXBlocks<TYPE>);
-        const int wi = threadIdx.x >> 5;
-        for (int ch = wi; ch < ng * 8; ch += kWarps) {
-            const float v = __ldcg(a.x_raw + int64_t(ch) * 32 + lane);
-            if constexpr (kXBlocks<TYPE> == 16)
-                prep_x32<16>(v, ch, lane, xb, sc, sm);
-            else
-                prep_x32<32>(v, ch, lane, xb, sc, sm);
-        }
-        if (threadIdx.x < kSlotBytes / 4) zs[threadIdx.x] = 0u;
-        __syncthreads();
-        xfrags = xb;
-        xzeros = reinterpret_cast<const uint8_t*>(zs);
-        xscale = sc;
-        xsum = sm;
-    }
-    using XL = typename std::conditional<kXS, LdShared, LdGlobal>::type;
-
     const bool supplier = g == t || g == t + 4;
-    const uint8_t* fb0 = supplier ? xfrags + g * kSlotBytes : xzeros;
+    const uint8_t* fb0 = supplier ? a.frags + g * kSlotBytes : a.zeros;
     const int fc = supplier ? kChunkFragBytes : 0;
     const int fg = supplier ? kGroupFragBytes : 0;
     int u = u0;
@@ -1206,16 +1162,16 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     ok = false;
                     break;
                 }
-                group_dot<TYPE, LdShared, LdGlobal>(ring + slot * UB, fb0 + gi * fg, fc, xscale + gi * kXBlocks<TYPE>,
-                                                    xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
+                group_dot<TYPE, LdShared, LdGlobal>(ring + slot * UB, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
+                                                    a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
                 __syncwarp();  // every lane has read the slot: refill it
                 if (lane == 0 && fu < u1) request(slot);
                 ++j;
             } else {
                 if (lane == 0 && tbeg + gi + kPrefetch < u1 && gi + kPrefetch < pf_end)
                     prefetch_l2(tw + (gi + kPrefetch) * kUnitBytes<TYPE>, kUnitBytes<TYPE>);
-                group_dot<TYPE, LdGlobal, XL>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, xscale + gi * kXBlocks<TYPE>,
-                                              xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
+                group_dot<TYPE>(tw + gi * kUnitBytes<TYPE>, fb0 + gi * fg, fc, a.scale + gi * kXBlocks<TYPE>,
+                                a.xsum + gi * kXBlocks<TYPE>, lane, g, t, y0, y8);
             }
         }
         if (!ok) break;
@@ -1271,7 +1227,6 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
                     if (lane < MMA_TILE_ROWS) a.partial[(cta * 2 + (tile == t0 ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
                     const int gprev = warp_count_in(a.count + tile);
                     if (gprev == cb - ca) {
-                        if (lane == 0) a.count[tile] = 0;  // every CTA counted in: clear for the slot's next launch
                         // lane (row r, half h) adds CTAs ca + h, ca + h + 2, ..., eight loads in flight
                         const int h = lane >> 4;
                         // CTA ca's first tile (unit mode only: in tile mode no tile spans CTAs)
@@ -1608,7 +1563,6 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
                 a.partial[(cta * 2 + (my_tile == first_tile ? 0 : 1)) * MMA_TILE_ROWS + r] = acc;
             const int prev = warp_count_in(a.count + my_tile);
             if (prev == cb - ca) {
-                if (lane == 0) a.count[my_tile] = 0;
                 float sum = 0.f;
                 if (lane < MMA_TILE_ROWS)
                     for (int c2 = ca; c2 <= cb; ++c2) {
@@ -2085,61 +2039,57 @@ cudaError_t mma_repack_launch(int type, const void* raw, void* packed, int64_t N
     return cudaGetLastError();
 }
 
-template <int TYPE, bool kTiles, bool kRing, bool kXS>
+template <int TYPE, bool kTiles, bool kRing>
 static cudaError_t launch_gemv_typed(cudaLaunchConfig_t& cg, const GemvArgs& a) {
-    if constexpr (kRing || kXS) {
+    if constexpr (kRing) {
         static std::atomic<size_t> smem_set[kMaxDevices];
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
         if (smem_set[dev].load() < cg.dynamicSmemBytes) {
-            e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, kTiles, kRing, kXS>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(cg.dynamicSmemBytes));
-            if (e == cudaSuccess && kRing) e = match_carveouts();
+            e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, kTiles, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(cg.dynamicSmemBytes));
+            if (e == cudaSuccess) e = match_carveouts();
             if (e != cudaSuccess) return e;
             smem_set[dev].store(cg.dynamicSmemBytes);
         }
     }
-    return cudaLaunchKernelEx(&cg, gemv_mma_kernel<TYPE, kTiles, kRing, kXS>, a);
+    return cudaLaunchKernelEx(&cg, gemv_mma_kernel<TYPE, kTiles, kRing>, a);
 }
 
 // Dynamic shared memory of gemv_mma_kernel for a launch touching cta_tiles
-// tiles per CTA: the partial rows and tile counters, then the ring variant's
-// rings and barriers, or the self-prepared x of a launch of ngroups groups.
-template <int TYPE>
-static size_t gemv_smem_typed(int cta_tiles, bool ring, bool xs, int64_t ngroups) {
+// tiles per CTA (the ring variant adds its rings and barriers).
+static size_t gemv_smem(int type, int cta_tiles, bool ring) {
     const size_t base = size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(cta_tiles) * sizeof(int);
-    if (ring) return ring_offset(cta_tiles) + ring_bytes<TYPE>();
-    if (xs) return ring_offset(cta_tiles) + xs_bytes<TYPE>(ngroups);
-    return base;
-}
-static size_t gemv_smem(int type, int cta_tiles, bool ring, bool xs, int64_t ngroups) {
+    if (!ring) return base;
+    size_t rb;
     switch (type) {
-        case T_Q4_K: return gemv_smem_typed<T_Q4_K>(cta_tiles, ring, xs, ngroups);
-        case T_Q5_K: return gemv_smem_typed<T_Q5_K>(cta_tiles, ring, xs, ngroups);
-        case T_Q6_K: return gemv_smem_typed<T_Q6_K>(cta_tiles, ring, xs, ngroups);
-        case T_Q3_K: return gemv_smem_typed<T_Q3_K>(cta_tiles, ring, xs, ngroups);
-        case T_IQ4_XS: return gemv_smem_typed<T_IQ4_XS>(cta_tiles, ring, xs, ngroups);
-        case T_IQ3_S: return gemv_smem_typed<T_IQ3_S>(cta_tiles, ring, xs, ngroups);
-        case T_IQ3_XXS: return gemv_smem_typed<T_IQ3_XXS>(cta_tiles, ring, xs, ngroups);
-        case T_IQ2_S: return gemv_smem_typed<T_IQ2_S>(cta_tiles, ring, xs, ngroups);
-        default: return gemv_smem_typed<T_Q4_0>(cta_tiles, ring, xs, ngroups);
+        case T_Q4_K: rb = ring_bytes<T_Q4_K>(); break;
+        case T_Q5_K: rb = ring_bytes<T_Q5_K>(); break;
+        case T_Q6_K: rb = ring_bytes<T_Q6_K>(); break;
+        case T_Q3_K: rb = ring_bytes<T_Q3_K>(); break;
+        case T_IQ4_XS: rb = ring_bytes<T_IQ4_XS>(); break;
+        case T_IQ3_S: rb = ring_bytes<T_IQ3_S>(); break;
+        case T_IQ3_XXS: rb = ring_bytes<T_IQ3_XXS>(); break;
+        case T_IQ2_S: rb = ring_bytes<T_IQ2_S>(); break;
+        default: rb = ring_bytes<T_Q4_0>(); break;
     }
+    return ring_offset(cta_tiles) + rb;
 }
 
-template <bool kTiles, bool kRing, bool kXS>
+template <bool kTiles, bool kRing>
 static cudaError_t launch_gemv(int type, cudaLaunchConfig_t& cg, const GemvArgs& a) {
     switch (type) {
-        case T_Q4_K: return launch_gemv_typed<T_Q4_K, kTiles, kRing, kXS>(cg, a);
-        case T_Q5_K: return launch_gemv_typed<T_Q5_K, kTiles, kRing, kXS>(cg, a);
-        case T_Q6_K: return launch_gemv_typed<T_Q6_K, kTiles, kRing, kXS>(cg, a);
-        case T_Q3_K: return launch_gemv_typed<T_Q3_K, kTiles, kRing, kXS>(cg, a);
-        case T_IQ4_XS: return launch_gemv_typed<T_IQ4_XS, kTiles, kRing, kXS>(cg, a);
-        case T_IQ3_S: return launch_gemv_typed<T_IQ3_S, kTiles, kRing, kXS>(cg, a);
-        case T_IQ3_XXS: return launch_gemv_typed<T_IQ3_XXS, kTiles, kRing, kXS>(cg, a);
-        case T_IQ2_S: return launch_gemv_typed<T_IQ2_S, kTiles, kRing, kXS>(cg, a);
-        default: return launch_gemv_typed<T_Q4_0, kTiles, kRing, kXS>(cg, a);
+        case T_Q4_K: return launch_gemv_typed<T_Q4_K, kTiles, kRing>(cg, a);
+        case T_Q5_K: return launch_gemv_typed<T_Q5_K, kTiles, kRing>(cg, a);
+        case T_Q6_K: return launch_gemv_typed<T_Q6_K, kTiles, kRing>(cg, a);
+        case T_Q3_K: return launch_gemv_typed<T_Q3_K, kTiles, kRing>(cg, a);
+        case T_IQ4_XS: return launch_gemv_typed<T_IQ4_XS, kTiles, kRing>(cg, a);
+        case T_IQ3_S: return launch_gemv_typed<T_IQ3_S, kTiles, kRing>(cg, a);
+        case T_IQ3_XXS: return launch_gemv_typed<T_IQ3_XXS, kTiles, kRing>(cg, a);
+        case T_IQ2_S: return launch_gemv_typed<T_IQ2_S, kTiles, kRing>(cg, a);
+        default: return launch_gemv_typed<T_Q4_0, kTiles, kRing>(cg, a);
     }
 }
 
@@ -2249,11 +2199,6 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     const size_t smem = size_t(kWarps) * 2 * MMA_TILE_ROWS * sizeof(float) + size_t(a.cta_tiles) * sizeof(int);
     if (smem > 48 * 1024) return cudaErrorInvalidValue;  // beyond any shape the layout admits
 
-    const int choice = classic ? 0 : gemv_kernel_choice();
-    if (xchg && (choice == 1 || choice == 2)) return cudaErrorInvalidValue;  // the bulk kernel has no exchange
-    // a local launch whose x no earlier launch prepared, of up to
-    // kXsMaxGroups groups: every CTA prepares x itself (no x-preparation kernel)
-    const bool self_prep = !x_ready && !xchg && !classic && choice == 0 && ngroups <= kXsMaxGroups;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
@@ -2266,7 +2211,7 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cp.stream = stream;
     cp.attrs = attr;
     cp.numAttrs = 1;
-    if (!x_ready && !self_prep) {  // else the previous launch's epilogue prepared x (and the counters are clear)
+    if (!x_ready) {  // else the previous launch's epilogue prepared x (and the counters are clear)
         cudaError_t e = mma_blk16(type)
                             ? cudaLaunchKernelEx(&cp, xprep_kernel<16>, x, K, base + L.frags, base + L.zeros,
                                                  reinterpret_cast<float*>(base + L.scale),
@@ -2277,6 +2222,8 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
         if (e != cudaSuccess) return e;
     }
 
+    const int choice = classic ? 0 : gemv_kernel_choice();
+    if (xchg && (choice == 1 || choice == 2)) return cudaErrorInvalidValue;  // the bulk kernel has no exchange
     if (choice == 1 || choice == 2) {
         bool used = false;
         const cudaError_t e = launch_bulk(type, choice == 2, a, ntiles, sms, stream, &used);
@@ -2288,22 +2235,15 @@ cudaError_t gemv_mma_multi_launch(int type, const MmaSegment* segs, int nseg, co
     cudaLaunchConfig_t cg = {};
     cg.gridDim = dim3(static_cast<unsigned>(blocks));
     cg.blockDim = dim3(kGemvThreads);
-    cg.dynamicSmemBytes = gemv_smem(type, a.cta_tiles, ring, self_prep, ngroups);
+    cg.dynamicSmemBytes = gemv_smem(type, a.cta_tiles, ring);
     cg.stream = stream;
     cudaLaunchAttribute attr2[1];
     attr2[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr2[0].val.programmaticStreamSerializationAllowed = 1;  // overlap the L2 warm-up with xprep
     cg.attrs = attr2;
     cg.numAttrs = 1;
-    if (ring)
-        return a.tile_mode ? launch_gemv<true, true, false>(type, cg, a) : launch_gemv<false, true, false>(type, cg, a);
-    if (self_prep) {
-        a.x_raw = x;
-        // with pdl the GEMV waits (griddepcontrol.wait) for the kernel before it, which may write x
-        attr2[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-        return a.tile_mode ? launch_gemv<true, false, true>(type, cg, a) : launch_gemv<false, false, true>(type, cg, a);
-    }
-    return a.tile_mode ? launch_gemv<true, false, false>(type, cg, a) : launch_gemv<false, false, false>(type, cg, a);
+    if (ring) return a.tile_mode ? launch_gemv<true, true>(type, cg, a) : launch_gemv<false, true>(type, cg, a);
+    return a.tile_mode ? launch_gemv<true, false>(type, cg, a) : launch_gemv<false, false>(type, cg, a);
 }
 
 cudaError_t xchg_gather_launch(const float* xdata, int64_t half_floats, const uint32_t* flags,
