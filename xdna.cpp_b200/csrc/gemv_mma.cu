@@ -633,23 +633,39 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
     y8 = fmaf(h2f(h8.x), fmaf(k6[1][0] * sc2.x, T[2], k6[1][1] * sc2.y * T[3]), y8);
 }
 
+// Grid lookups of the IQ3 formats go to shared memory at random entries, and
+// 32 lanes reading random words of one table conflict on its banks (about 4
+// wavefronts per load instead of 1).  So each CTA holds several copies of a
+// grid, interleaved word by word: entry e of copy j sits at word
+// e * copies + j, and lane l reads copy l % copies, in bank l % 32 when there
+// are 32 copies.  Static shared memory stops at 48 KiB per CTA: IQ3_XXS
+// (256 entries) gets 32 copies, IQ3_S (512 entries) 16 (two lanes per bank),
+// in 32 KiB each.
+constexpr int kIq3sCopies = 16;
+constexpr int kIq3xxsCopies = 32;
+template <int TYPE>
+constexpr size_t kGridSmem = TYPE == T_IQ3_S     ? 512 * kIq3sCopies * 4
+                             : TYPE == T_IQ3_XXS ? 256 * kIq3xxsCopies * 4
+                             : TYPE == T_IQ2_S   ? 1024 * 8
+                                                 : 0;
+
 // IQ3_S: value = d * (1 + 2 s) * grid[idx] * sign with a 4-bit s per 32
 // values (ggml-quants.c dequantize_row_iq3_s).  Each A register is one grid
-// entry (4 unsigned magnitudes 1..15) read from the CTA's shared copy of the
+// entry (4 unsigned magnitudes 1..15) read from the lane's copy of the
 // 512-entry grid, with its 4 sign bits applied per byte: the bits are spread
 // to the bytes' top bits by a multiply, prmt's sign-replicate mode widens
 // them to 0x00 / 0xFF masks m, and (g ^ m) + (m & 1) negates the masked bytes
 // (no carry between bytes: every magnitude is at least 1).
-__shared__ uint32_t s_iq3s_grid[512];
+__shared__ uint32_t s_iq3s_grid[512 * kIq3sCopies];
 
 // four unsigned magnitudes g (each >= 1) with 4 sign bits applied, as s8
 __device__ __forceinline__ uint32_t signed4(uint32_t g, uint32_t s4) {
     const uint32_t m = prmt(s4 * 0x10204080u, 0u, 0xBA98u);
     return (g ^ m) + (m & 0x01010101u);
 }
-__device__ __forceinline__ uint32_t iq3s_reg(uint32_t iw, uint32_t hw, uint32_t sw, int k) {
+__device__ __forceinline__ uint32_t iq3s_reg(uint32_t iw, uint32_t hw, uint32_t sw, int k, int lane) {
     const uint32_t idx = ((iw >> (8 * k)) & 0xFFu) | (((hw >> k) & 1u) << 8);
-    return signed4(s_iq3s_grid[idx], (sw >> (4 * k)) & 0xFu);
+    return signed4(s_iq3s_grid[idx * kIq3sCopies + (lane & (kIq3sCopies - 1))], (sw >> (4 * k)) & 0xFu);
 }
 
 template <class W, class X>
@@ -675,8 +691,8 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
         const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
         const uint32_t sw = word(S, c >> 1) >> (16 * (c & 1));
         const uint32_t hw = qh >> (4 * c);
-        const uint32_t a0 = iq3s_reg(iw, hw, sw, 0), a1 = iq3s_reg(iw, hw, sw, 1);
-        const uint32_t a2 = iq3s_reg(iw, hw, sw, 2), a3 = iq3s_reg(iw, hw, sw, 3);
+        const uint32_t a0 = iq3s_reg(iw, hw, sw, 0, lane), a1 = iq3s_reg(iw, hw, sw, 1, lane);
+        const uint32_t a2 = iq3s_reg(iw, hw, sw, 2, lane), a3 = iq3s_reg(iw, hw, sw, 3, lane);
         mma_s8s8(C[0], a0, a1, a2, a3, q.x, q.y);
         mma_s8s8(C[1], a0, a1, a2, a3, q.z, q.w);
         mma_s8s8(C[2], a0, a1, a2, a3, r.x, r.y);
@@ -697,9 +713,10 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
 
 // IQ3_XXS: value = d * (0.5 + s) / 2 * grid[q] * sign with a 4-bit s per 32
 // values (gguf quants.py IQ3_XXS).  As IQ3_S, one shared-memory grid entry
-// (256 entries, magnitudes 4..62) per A register; the 8 signs of 8 values
-// are a 7-bit index plus the bit that makes the count of negatives even.
-__shared__ uint32_t s_iq3xxs_grid[256];
+// (256 entries, magnitudes 4..62, one copy per lane) per A register; the 8
+// signs of 8 values are a 7-bit index plus the bit that makes the count of
+// negatives even.
+__shared__ uint32_t s_iq3xxs_grid[256 * kIq3xxsCopies];
 
 template <class W, class X>
 __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_t* fb, int fc,
@@ -725,7 +742,7 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
         for (int k = 0; k < 4; ++k) {
             const uint32_t si = (w >> (7 * k)) & 127u;
             const uint32_t sb = si | ((__popc(si) & 1u) << 7);
-            a[k] = signed4(s_iq3xxs_grid[(iw >> (8 * k)) & 0xFFu], (sb >> (4 * (c & 1))) & 0xFu);
+            a[k] = signed4(s_iq3xxs_grid[((iw >> (8 * k)) & 0xFFu) * kIq3xxsCopies + lane], (sb >> (4 * (c & 1))) & 0xFu);
         }
         mma_s8s8(C[0], a[0], a[1], a[2], a[3], q.x, q.y);
         mma_s8s8(C[1], a[0], a[1], a[2], a[3], q.z, q.w);
@@ -978,8 +995,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // Per-warp shared-memory ring of gemv_mma_kernel's ring variant: depth (in
 // units) per format, sized so that the 24 warps' rings take about 170 KiB.
 template <int TYPE>
-constexpr int kRingDepth = (170 * 1024) / (kWarps * kUnitBytes<TYPE>) > 4 ? 4
-                                                                        : (170 * 1024) / (kWarps * kUnitBytes<TYPE>);
+constexpr int kRingDepth = (170 * 1024 - kGridSmem<TYPE>) / (kWarps * kUnitBytes<TYPE>) > 4
+                               ? 4
+                               : ((170 * 1024 - kGridSmem<TYPE>) / (kWarps * kUnitBytes<TYPE>) < 1
+                                      ? 1
+                                      : (170 * 1024 - kGridSmem<TYPE>) / (kWarps * kUnitBytes<TYPE>));
 // Bytes of the ring variant's dynamic shared memory after the partial rows
 // and tile counters (offset `off`): the rings, then their barriers.
 template <int TYPE>
@@ -1046,9 +1066,10 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         if (threadIdx.x == 0) s_abort = 0;
     }
     if constexpr (TYPE == T_IQ3_S)
-        for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
+        for (int i = threadIdx.x; i < 512 * kIq3sCopies; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i / kIq3sCopies];
     if constexpr (TYPE == T_IQ3_XXS)
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_iq3xxs_grid[i] = kIq3xxsGrid[i];
+        for (int i = threadIdx.x; i < 256 * kIq3xxsCopies; i += blockDim.x)
+            s_iq3xxs_grid[i] = kIq3xxsGrid[i / kIq3xxsCopies];
     if constexpr (TYPE == T_IQ2_S)
         for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s_grid[i] = kIq2sGrid[i];
     __syncthreads();
@@ -1376,9 +1397,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
     }
     if (threadIdx.x < kSlotBytes / 4) s_zero[threadIdx.x] = 0u;
     if constexpr (TYPE == T_IQ3_S)
-        for (int i = threadIdx.x; i < 512; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i];
+        for (int i = threadIdx.x; i < 512 * kIq3sCopies; i += blockDim.x) s_iq3s_grid[i] = kIq3sGrid[i / kIq3sCopies];
     if constexpr (TYPE == T_IQ3_XXS)
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) s_iq3xxs_grid[i] = kIq3xxsGrid[i];
+        for (int i = threadIdx.x; i < 256 * kIq3xxsCopies; i += blockDim.x)
+            s_iq3xxs_grid[i] = kIq3xxsGrid[i / kIq3xxsCopies];
     if constexpr (TYPE == T_IQ2_S)
         for (int i = threadIdx.x; i < 1024; i += blockDim.x) s_iq2s_grid[i] = kIq2sGrid[i];
     __syncthreads();
@@ -1906,7 +1928,7 @@ template <int TYPE>
 static bool bulk_plan(bool staged_x, int64_t ngroups, int64_t ntiles, int sms, BulkPlan* p) {
     constexpr int UB = kUnitBytes<TYPE>;
     // shared memory per CTA (227 KiB) less the static grid table of the IQ formats
-    constexpr size_t kGrid = TYPE == T_IQ2_S ? 8192 : (TYPE == T_IQ3_S ? 2048 : (TYPE == T_IQ3_XXS ? 1024 : 0));
+    constexpr size_t kGrid = kGridSmem<TYPE>;
     const size_t budget = 227 * 1024 - kGrid - 1024;
     BulkArgs& b = p->b;
     b = BulkArgs{};
