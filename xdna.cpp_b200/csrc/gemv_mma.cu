@@ -108,7 +108,7 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //           Block b < 4 is supplied by lane (g = b, t = b) in register b0,
 //           block b >= 4 by lane (g = b, t = b - 4) in register b1; the other
 //           register of the pair is zero, so the kernel needs no selects.
-//   zeros   32 zero bytes: the B "slot" of the 24 lanes that supply nothing
+//   zeros   kZeroBytes of zeros: the B "slots" of the 24 lanes that supply nothing
 //   scale   2^e per 32-value block;  xsum  sum of the block's x
 //   count   one arrival counter per tile, the CTA completion counter and one
 //           per 32-value chunk of a feeding output (cleared by xprep_kernel,
@@ -127,6 +127,11 @@ constexpr int kPrefetch = 2;         // groups ahead per warp (bulk L2 prefetch;
 constexpr int kSlotBytes = 32;
 constexpr int kChunkFragBytes = 8 * kSlotBytes;       // 8 blocks
 constexpr int kGroupFragBytes = 8 * kChunkFragBytes;  // 8 chunks: 2 KiB per 256 values
+// The zero B fragments of the 24 lanes that supply no x block: one group's
+// worth of zero slots, so that those lanes step through it with the same
+// constant chunk stride as the supplying lanes through the x fragments, and
+// every fragment load of a group takes an immediate offset from one address.
+constexpr int kZeroBytes = kGroupFragBytes;
 
 __device__ __forceinline__ uint32_t digit_word(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, int plane) {
     // byte `plane` of each of four lanes' packed digits, in value order
@@ -232,7 +237,7 @@ __global__ void __launch_bounds__(64) xprep_kernel(const float* __restrict__ x, 
     const int64_t gtid = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
     const int64_t nthr = int64_t(gridDim.x) * blockDim.x;
     for (int64_t i = gtid; i < ncount; i += nthr) count[i] = 0;
-    if (gtid < kSlotBytes / 4) reinterpret_cast<uint32_t*>(zeros)[gtid] = 0u;
+    for (int64_t i = gtid; i < kZeroBytes / 4; i += nthr) reinterpret_cast<uint32_t*>(zeros)[i] = 0u;
     const int lane = threadIdx.x & 31;
     const int64_t nw = K / 32;
     for (int64_t w32 = gtid >> 5; w32 < nw; w32 += nthr >> 5) prep_x32<BL>(x[w32 * 32 + lane], w32, lane, frags, scale, xsum);
@@ -1115,7 +1120,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
         // scratch slot's previous user has completed (this launch waited on it)
         const int64_t gt = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
         for (int64_t i = gt; i < a.f_ncount; i += int64_t(gridDim.x) * blockDim.x) a.f_count[i] = 0;
-        if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
+        for (int64_t i = gt; i < kZeroBytes / 4; i += int64_t(gridDim.x) * blockDim.x) a.f_zeros[i] = 0u;
     }
     if (a.wait_peers) {
         // Sharded chain: part of this launch's x was prepared by the peers
@@ -1160,7 +1165,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_mma_kernel(cons
 
     const bool supplier = g == t || g == t + 4;
     const uint8_t* fb0 = supplier ? a.frags + g * kSlotBytes : a.zeros;
-    const int fc = supplier ? kChunkFragBytes : 0;
+    constexpr int fc = kChunkFragBytes;  // the zero lanes step through kZeroBytes of zeros
     const int fg = supplier ? kGroupFragBytes : 0;
     int u = u0;
     int j = 0;  // units this warp has consumed (ring slot and phase)
@@ -1496,7 +1501,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const GemvAr
     if (a.f_bl != 0) {
         const int64_t gt = int64_t(cta) * (kCons * 32) + ctid;
         for (int64_t i = gt; i < a.f_ncount; i += int64_t(G) * (kCons * 32)) a.f_count[i] = 0;
-        if (gt < kSlotBytes / 4) a.f_zeros[gt] = 0u;
+        for (int64_t i = gt; i < kZeroBytes / 4; i += int64_t(G) * (kCons * 32)) a.f_zeros[i] = 0u;
     }
     const bool supplier = g == t || g == t + 4;
     const int fc = supplier ? kChunkFragBytes : 0;
@@ -1675,7 +1680,7 @@ __global__ void __launch_bounds__(256) xchg_gather_kernel(const float* __restric
     const int64_t stride = int64_t(gridDim.x) * blockDim.x;
     if (f.bl != 0) {
         for (int64_t i = gt; i < f.ncount; i += stride) f.count[i] = 0;
-        if (gt < kSlotBytes / 4) f.zeros[gt] = 0u;
+        for (int64_t i = gt; i < kZeroBytes / 4; i += stride) f.zeros[i] = 0u;
     }
     for (int s = 0; s < g.nseg; ++s) {
         const GatherSeg sg = g.seg[s];
@@ -1845,7 +1850,7 @@ ScratchLayout scratch_layout(int64_t N, int64_t K) {
     const size_t ntiles = static_cast<size_t>(N / MMA_TILE_ROWS);
     L.frags = 0;
     L.zeros = up(L.frags + ngroups * kGroupFragBytes);
-    L.scale = up(L.zeros + kSlotBytes);
+    L.scale = up(L.zeros + kZeroBytes);
     L.xsum = up(L.scale + 2 * nblk * sizeof(float));  // room for 16-value blocks
     L.count = up(L.xsum + 2 * nblk * sizeof(float));
     L.partial = up(L.count + counter_ints(static_cast<int64_t>(ntiles)) * sizeof(int));
