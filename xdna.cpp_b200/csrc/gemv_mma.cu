@@ -104,7 +104,10 @@ __device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, 
 //
 // Scratch of one launch (all offsets 256-byte aligned):
 //   frags   per group, per chunk c (32 values of each of the 8 blocks), per
-//           block b: a 32-byte B-fragment slot {b0,b1} x 3 digit planes.
+//           block b: a 32-byte B-fragment slot: {b0,b1} of digit planes 0
+//           and 1, then, in an even chunk's slot, {b0,b1} of plane 2 of
+//           this chunk and of the next (an odd chunk's last 16 bytes are
+//           unused), so a chunk pair takes three 16-byte loads.
 //           Block b < 4 is supplied by lane (g = b, t = b) in register b0,
 //           block b >= 4 by lane (g = b, t = b - 4) in register b1; the other
 //           register of the pair is zero, so the kernel needs no selects.
@@ -198,17 +201,20 @@ __device__ __forceinline__ void prep_x32(float v, int64_t w32, int lane, uint8_t
         const int jb = static_cast<int>(b % kPerGroup);
         const int blk = jb & 7;                                          // B column
         const int c = (BL == 32 ? 0 : 4 * (jb >> 3)) + (lane % BL) / 4;  // chunk
-        uint4* slot = reinterpret_cast<uint4*>(frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes);
+        // planes 0 and 1 to the chunk's slot; plane 2 to the last 16 bytes of
+        // the chunk pair's even slot, first half for the even chunk (load_b)
+        uint8_t* sb = frags + gi * kGroupFragBytes + c * kChunkFragBytes + blk * kSlotBytes;
+        uint4* slot = reinterpret_cast<uint4*>(sb);
+        uint2* p2 = reinterpret_cast<uint2*>((c & 1) ? sb - kChunkFragBytes + 24 : sb + 16);
         const uint4 s0 = blk < 4 ? make_uint4(D0, 0u, D1, 0u) : make_uint4(0u, D0, 0u, D1);
-        const uint4 s1 = blk < 4 ? make_uint4(D2, 0u, 0u, 0u) : make_uint4(0u, D2, 0u, 0u);
-        slot[0] = s0;
-        slot[1] = s1;
+        const uint2 s1 = blk < 4 ? make_uint2(D2, 0u) : make_uint2(0u, D2);
+        *slot = s0;
+        *p2 = s1;
         if (pd.pb)
             for (int p = 0; p < pd.world; ++p)
                 if (p != pd.rank) {
-                    uint4* ps = at_peer(pd, p, slot);
-                    ps[0] = s0;
-                    ps[1] = s1;
+                    *at_peer(pd, p, slot) = s0;
+                    *at_peer(pd, p, p2) = s1;
                 }
     }
     if (lane % BL == 0) {
@@ -449,6 +455,17 @@ struct LdShared {
     static __device__ __forceinline__ uint32_t h(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
 };
 
+// B fragments of chunk c: planes 0 and 1 (q) from the chunk's slot, plane 2
+// (r) from the slot of the chunk pair's even member, whose last 16 bytes
+// hold plane 2 of both chunks (r2, loaded at the even chunk and kept for the
+// odd one): three 16-byte loads per chunk pair.
+template <class X>
+__device__ __forceinline__ void load_b(const uint8_t* fb, int c, int fc, uint4& q, uint2& r, uint4& r2) {
+    q = X::q_ro(fb + c * fc);
+    if ((c & 1) == 0) r2 = X::q_ro(fb + c * fc + 16);
+    r = (c & 1) ? make_uint2(r2.z, r2.w) : make_uint2(r2.x, r2.y);
+}
+
 // One group of 16 rows x 256 values: accumulate rows g and g+8 of this lane.
 // fb: this lane's B slot of chunk 0 (or the zero slot), fc: bytes between chunks.
 // Q6_K: two sets of 8 sixteen-value blocks; q = 6 bits (A = q, u8), value =
@@ -473,11 +490,13 @@ __device__ __forceinline__ void group_dot_q6k(const uint8_t* gb, const uint8_t* 
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int k = 0; k < 4; ++k) C[p][k] = 0;
+        uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
         for (int cs = 0; cs < 4; ++cs) {
             const int c = 4 * st + cs;
-            const uint4 q = X::q_ro(fb + c * fc);
-            const uint2 r = X::d(fb + c * fc + 16);
+            uint4 q;
+            uint2 r;
+            load_b<X>(fb, c, fc, q, r, r2);
             const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
             const uint32_t hw = word(H[c >> 2], c & 3);  // bits 8j + 2k: high pair of register k
             const uint32_t a0 = (w0 & 0x0F0F0F0Fu) | ((hw << 4) & 0x30303030u);
@@ -525,11 +544,13 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
         for (int p = 0; p < 3; ++p)
 #pragma unroll
             for (int k = 0; k < 4; ++k) C[p][k] = 0;
+        uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
         for (int cs = 0; cs < 4; ++cs) {
             const int c = 4 * st + cs;
-            const uint4 q = X::q_ro(fb + c * fc);
-            const uint2 r = X::d(fb + c * fc + 16);
+            uint4 q;
+            uint2 r;
+            load_b<X>(fb, c, fc, q, r, r2);
             const uint32_t lw = word(c < 4 ? L0 : L1, c & 3);  // bits 8j + 2k: low pair of register k
             const uint32_t hw = word(H, c >> 1);                // bit 8j + 4 (c & 1) + k: high bit
             uint32_t hk[4];
@@ -604,10 +625,12 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
     for (int p = 0; p < 3; ++p)
 #pragma unroll
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
+    uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = X::q_ro(fb + c * fc);
-        const uint2 r = X::d(fb + c * fc + 16);
+        uint4 q;
+        uint2 r;
+        load_b<X>(fb, c, fc, q, r, r2);
         uint32_t a0, a1, a2, a3;
         iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1)), a0, a1);
         iq4nl_lookup2(word(A[c >> 1], 2 * (c & 1) + 1), a2, a3);
@@ -689,10 +712,12 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
     for (int p = 0; p < 3; ++p)
 #pragma unroll
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
+    uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = X::q_ro(fb + c * fc);
-        const uint2 r = X::d(fb + c * fc + 16);
+        uint4 q;
+        uint2 r;
+        load_b<X>(fb, c, fc, q, r, r2);
         const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
         const uint32_t sw = word(S, c >> 1) >> (16 * (c & 1));
         const uint32_t hw = qh >> (4 * c);
@@ -736,10 +761,12 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
     for (int p = 0; p < 3; ++p)
 #pragma unroll
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
+    uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = X::q_ro(fb + c * fc);
-        const uint2 r = X::d(fb + c * fc + 16);
+        uint4 q;
+        uint2 r;
+        load_b<X>(fb, c, fc, q, r, r2);
         const uint32_t iw = word(c < 4 ? I0 : I1, c & 3);
         const uint32_t w = word(SS, c >> 1);
         uint32_t a[4];
@@ -804,11 +831,13 @@ __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t*
                 lo[k] = signed4(static_cast<uint32_t>(gv), sb & 0xFu);
                 hi[k] = signed4(static_cast<uint32_t>(gv >> 32), sb >> 4);
             }
+            uint4 r2;  // plane 2 of the chunk pair (c = 4 st + 2 qq, + 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int c = 4 * st + 2 * qq + h;
-                const uint4 bq = X::q_ro(fb + c * fc);
-                const uint2 br = X::d(fb + c * fc + 16);
+                uint4 bq;
+                uint2 br;
+                load_b<X>(fb, c, fc, bq, br, r2);
                 const uint32_t* a = h ? hi : lo;
                 mma_s8s8(C[0], a[0], a[1], a[2], a[3], bq.x, bq.y);
                 mma_s8s8(C[1], a[0], a[1], a[2], a[3], bq.z, bq.w);
@@ -854,10 +883,12 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
     for (int p = 0; p < 3; ++p)
 #pragma unroll
         for (int k = 0; k < 4; ++k) C[p][k] = 0;
+    uint4 r2;  // plane 2 of the current chunk pair
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        const uint4 q = X::q_ro(fb + c * fc);
-        const uint2 r = X::d(fb + c * fc + 16);
+        uint4 q;
+        uint2 r;
+        load_b<X>(fb, c, fc, q, r, r2);
         const uint32_t w0 = word(A[c >> 1], 2 * (c & 1)), w1 = word(A[c >> 1], 2 * (c & 1) + 1);
         uint32_t a0, a1, a2, a3;
         if (TYPE == T_Q5_K) {
