@@ -455,6 +455,14 @@ struct LdShared {
     static __device__ __forceinline__ uint32_t h(const uint8_t* p) { return *reinterpret_cast<const unsigned short*>(p); }
 };
 
+// Byte permute (prmt.b32): result byte i is byte sel[4i+2:4i] of {b, a}
+// (a = bytes 0-3), or that byte's sign replicated when sel[4i+3] is set.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
 // B fragments of chunk c: planes 0 and 1 (q) from the chunk's slot, plane 2
 // (r) from the slot of the chunk pair's even member, whose last 16 bytes
 // hold plane 2 of both chunks (r2, loaded at the even chunk and kept for the
@@ -600,11 +608,6 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
 // lookup (code ^ 8) gives 0, for a code of 8 or more the XA lookup gives the
 // pair's sign, and the XOR of the two lookups is the value either way.
 // Each code word holds registers (k, k+1) as 16-bit selector halves.
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
 __device__ __forceinline__ void iq4nl_lookup2(uint32_t w, uint32_t& lo, uint32_t& hi) {
     const uint32_t x = w ^ 0x88888888u;
     lo = prmt(XB_IQ4NL_XA_0, XB_IQ4NL_XA_1, w) ^ prmt(XB_IQ4NL_XB_0, XB_IQ4NL_XB_1, x);
@@ -933,8 +936,10 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
     const float2 xs2 = __ldg(reinterpret_cast<const float2*>(xs_) + t);
     const float s0 = sc2.x, s1 = sc2.y, x0 = xs2.x, x1 = xs2.y;
     if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four per word
-        const int sh = 16 * (t & 1);
+        // six-bit scales / mins of sub-blocks 2t, 2t+1 (kquants.h:204-212), four
+        // per word; byte k of a word becomes a float as 2^23 + byte (prmt into
+        // the exponent 0x4B) less 2^23, exactly, without the conversion pipe
+        const uint32_t sel = 0x7540u | (2u * static_cast<uint32_t>(t & 1));
         float sc[2][2], mn[2][2], d[2], dm[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -942,10 +947,10 @@ __device__ __forceinline__ void group_dot_nib(const uint8_t* gb, const uint8_t* 
             const uint32_t scw = t < 2 ? (hh.y & 0x3F3F3F3Fu) : ((hh.w & 0x0F0F0F0Fu) | ((hh.y >> 2) & 0x30303030u));
             const uint32_t mw = t < 2 ? (hh.z & 0x3F3F3F3Fu)
                                       : (((hh.w >> 4) & 0x0F0F0F0Fu) | ((hh.z >> 2) & 0x30303030u));
-            sc[h][0] = static_cast<float>((scw >> sh) & 0xFFu);
-            sc[h][1] = static_cast<float>((scw >> (sh + 8)) & 0xFFu);
-            mn[h][0] = static_cast<float>((mw >> sh) & 0xFFu);
-            mn[h][1] = static_cast<float>((mw >> (sh + 8)) & 0xFFu);
+            sc[h][0] = __int_as_float(prmt(scw, 0x4B000000u, sel)) - 8388608.0f;
+            sc[h][1] = __int_as_float(prmt(scw, 0x4B000000u, sel + 1)) - 8388608.0f;
+            mn[h][0] = __int_as_float(prmt(mw, 0x4B000000u, sel)) - 8388608.0f;
+            mn[h][1] = __int_as_float(prmt(mw, 0x4B000000u, sel + 1)) - 8388608.0f;
             d[h] = h2f(hh.x);
             dm[h] = h2f(hh.x >> 16);
         }
