@@ -59,6 +59,9 @@ __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
     return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
 }
+// An integer 0 <= v < 2^23 as a float, exactly: its bits under the exponent
+// of 2^23, less 2^23 (a logic and a float instruction; no conversion pipe).
+__device__ __forceinline__ float u23f(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388608.0f; }
 __device__ __forceinline__ float h2f(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu)));
 }
@@ -590,7 +593,7 @@ __device__ __forceinline__ void group_dot_q3k(const uint8_t* gb, const uint8_t* 
         for (int hb = 0; hb < 4; ++hb) {
             const int i = 4 * (hb >> 1) + 2 * st + (hb & 1);
             const uint32_t v = ((slo >> (4 * i)) & 0xFu) | (((shi >> (2 * i)) & 3u) << 4);
-            k6[hb] = static_cast<float>(static_cast<int>(v) - 32);
+            k6[hb] = u23f(v) - 32.0f;
         }
         const float b0 = -4.0f * xs2.x, b1 = -4.0f * xs2.y;
         y0 = fmaf(dg, fmaf(k6[0], fmaf(sc2.x, T[0], b0), k6[1] * fmaf(sc2.y, T[1], b1)), y0);
@@ -657,7 +660,7 @@ __device__ __forceinline__ void group_dot_iq4xs(const uint8_t* gb, const uint8_t
         for (int b = 0; b < 2; ++b) {
             const int ib = 2 * t + b;
             const uint32_t ls = ((hh.y >> (4 * ib)) & 0xFu) | (((hh.x >> (16 + 2 * ib)) & 3u) << 4);
-            k6[h][b] = static_cast<float>(static_cast<int>(ls) - 32);
+            k6[h][b] = u23f(ls) - 32.0f;
         }
     }
     y0 = fmaf(h2f(h0.x), fmaf(k6[0][0] * sc2.x, T[0], k6[0][1] * sc2.y * T[1]), y0);
@@ -738,8 +741,8 @@ __device__ __forceinline__ void group_dot_iq3s(const uint8_t* gb, const uint8_t*
     const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     // scales of blocks 2t (low nibble) and 2t + 1 (high nibble) are byte t of the row's scales
     const uint32_t bg = (sg >> (8 * t)) & 0xFFu, b8 = (s8 >> (8 * t)) & 0xFFu;
-    const float kg0 = static_cast<float>(1 + 2 * (bg & 0xFu)), kg1 = static_cast<float>(1 + 2 * (bg >> 4));
-    const float k80 = static_cast<float>(1 + 2 * (b8 & 0xFu)), k81 = static_cast<float>(1 + 2 * (b8 >> 4));
+    const float kg0 = u23f(2u * (bg & 0xFu) + 1u), kg1 = u23f(2u * (bg >> 4) + 1u);
+    const float k80 = u23f(2u * (b8 & 0xFu) + 1u), k81 = u23f(2u * (b8 >> 4) + 1u);
     y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
     y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
 }
@@ -790,10 +793,10 @@ __device__ __forceinline__ void group_dot_iq3xxs(const uint8_t* gb, const uint8_
         T[k] = fmaf(static_cast<float>(C[2][k]), 65536.0f, static_cast<float>(C[1][k] * 256 + C[0][k]));
     const float2 sc2 = __ldg(reinterpret_cast<const float2*>(sc_) + t);
     // scales (top nibble of word p): p = 0 (g, 2t), 1 (g+8, 2t), 2 (g, 2t+1), 3 (g+8, 2t+1)
-    const float kg0 = 0.5f * (0.5f + static_cast<float>(SS.x >> 28));
-    const float k80 = 0.5f * (0.5f + static_cast<float>(SS.y >> 28));
-    const float kg1 = 0.5f * (0.5f + static_cast<float>(SS.z >> 28));
-    const float k81 = 0.5f * (0.5f + static_cast<float>(SS.w >> 28));
+    const float kg0 = 0.5f * (0.5f + u23f(SS.x >> 28));
+    const float k80 = 0.5f * (0.5f + u23f(SS.y >> 28));
+    const float kg1 = 0.5f * (0.5f + u23f(SS.z >> 28));
+    const float k81 = 0.5f * (0.5f + u23f(SS.w >> 28));
     y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
     y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
 }
@@ -855,10 +858,10 @@ __device__ __forceinline__ void group_dot_iq2s(const uint8_t* gb, const uint8_t*
         const float2 sc2 = reinterpret_cast<const float2*>(sc_ + 8 * st)[t];
         // nibble 4 st + 2 h + b: row g + 8 h, block 8 st + 2 t + b
         const uint32_t n = scw >> (16 * st);
-        const float kg0 = 0.25f * (0.5f + static_cast<float>(n & 0xFu));
-        const float kg1 = 0.25f * (0.5f + static_cast<float>((n >> 4) & 0xFu));
-        const float k80 = 0.25f * (0.5f + static_cast<float>((n >> 8) & 0xFu));
-        const float k81 = 0.25f * (0.5f + static_cast<float>((n >> 12) & 0xFu));
+        const float kg0 = 0.25f * (0.5f + u23f(n & 0xFu));
+        const float kg1 = 0.25f * (0.5f + u23f((n >> 4) & 0xFu));
+        const float k80 = 0.25f * (0.5f + u23f((n >> 8) & 0xFu));
+        const float k81 = 0.25f * (0.5f + u23f((n >> 12) & 0xFu));
         y0 = fmaf(dg, fmaf(kg0 * sc2.x, T[0], kg1 * sc2.y * T[1]), y0);
         y8 = fmaf(d8, fmaf(k80 * sc2.x, T[2], k81 * sc2.y * T[3]), y8);
     }
