@@ -510,3 +510,44 @@ def test_compute_graph_replays_repeated_device_lists(cuda, G, O):
             for i in range(len(lst)):
                 check_parity(ys[i].cpu().numpy(), O.gemv(shapes[i][1], raws[i], shapes[i][0], K, x), f"call {call} node {i}")
         buf.free()
+
+
+def test_compute_graph_pinned_host_input_and_output(cuda, G, O):
+    """A chain whose first input and last output sit in page-locked host
+    memory (a decode step's token vector and logits): compute_graph runs it on
+    device copies of those two operands, so the list is fused, chained and,
+    from its second call, replayed as a CUDA graph.  Three calls with a new
+    input in the same host buffer (eager, captured, replayed); every node
+    against the oracle on its actual input each time, and the host output
+    equal to the device-side result."""
+    torch = cuda
+    chain = [("a0", "Q4_K", 1024, "h0"), ("a1", "Q4_K", 512, "h0"), ("b", "Q4_K", 768, "a0"),
+             ("c", "Q6_K", 512, "b")]
+    dims = {"h0": 2048}
+    for out, _, N, _ in chain:
+        dims[out] = N
+    raws = {out: O.quantize(G.CLAIMED[t], normal_weights(N, dims[src], seed=1300 + i), nthreads=4)
+            for i, (out, t, N, src) in enumerate(chain)}
+    h_host = torch.empty(dims["h0"], dtype=torch.float32, pin_memory=True)
+    out_host = torch.empty(dims["c"], dtype=torch.float32, pin_memory=True)
+    with G.Backend(0) as be:
+        buf = G.Buffer(sum(r.nbytes for r in raws.values()) + 16 * 8192, dev=0)
+        acts = {k: torch.zeros(n, dtype=torch.float32, device="cuda") for k, n in dims.items() if k not in ("h0", "c")}
+        nodes = []
+        for out, t, N, src in chain:
+            w = buf.alloc(G.tensor(G.CLAIMED[t], [dims[src], N, 1, 1]))
+            buf.set(w, _np_ptr(raws[out]), 0, raws[out].nbytes)
+            xp = h_host.data_ptr() if src == "h0" else acts[src].data_ptr()
+            yp = out_host.data_ptr() if out == "c" else acts[out].data_ptr()
+            xt = G.tensor(G.F32, [dims[src], 1, 1, 1], data=xp)
+            nodes.append(G.mul_mat_node(w, xt, yp, N, name=out))
+        for call in range(3):
+            h = normal_x(dims["h0"], seed=1400 + call)
+            h_host.copy_(torch.from_numpy(h))
+            assert be.compute(nodes), G.last_error()
+            be.synchronize()
+            got = {k: v.cpu().numpy() for k, v in acts.items()}
+            got["h0"], got["c"] = h, out_host.numpy().copy()
+            for out, t, N, src in chain:
+                check_parity(got[out], O.gemv(G.CLAIMED[t], raws[out], N, dims[src], got[src]), f"call {call} {out}")
+        buf.free()

@@ -329,6 +329,15 @@ struct Backend {
     // x scratch it captured is reallocated.
     std::vector<uint64_t> graph_sig;
     bool graph_ok_sig = false;  // graph_sig was checked and is capturable
+    // Device copies of MUL_MAT inputs and outputs that sit in page-locked host
+    // memory (see shadow_host_operands); kept across calls, freed with the
+    // backend or when more than kMaxShadows would be needed.
+    struct HostShadow {
+        void* host;
+        size_t bytes;
+        void* dev;
+    };
+    std::vector<HostShadow> shadows;
     cudaGraphExec_t graph_exec = nullptr;
     uint64_t graph_gen = 0, scratch_gen = 0;
 };
@@ -1145,6 +1154,110 @@ void drop_graph(Backend* be) {
     be->graph_exec = nullptr;
 }
 
+bool is_pinned_host(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+// A node list whose MUL_MAT inputs or outputs are single F32 rows in
+// page-locked host memory (a decode step's token input and logits, say) is
+// run on a copy of the list in which those operands are device buffers: the
+// inputs are copied in at the start of the call and the outputs out at its
+// end.  The copy then plans, fuses, chains and replays as a CUDA graph like a
+// device-resident list, instead of staging every such node through the
+// host (page-locked copies are stream operations that a graph can hold).
+// Not used when a host range is both written and read by the list, or when
+// an operand is not one contiguous row.
+struct ShadowPlan {
+    std::vector<ggml_tensor_xdna> nodes, srcs;
+    std::vector<ggml_tensor_xdna*> ptrs;
+    std::vector<size_t> in, out;  // indices into Backend::shadows
+};
+constexpr size_t kMaxShadows = 64;
+
+bool shadow_host_operands(Backend* be, ggml_tensor_xdna** nodes, size_t n, bool may_alloc, ShadowPlan* sp) {
+    struct Use {
+        void* host;
+        size_t bytes;
+        bool out;
+    };
+    std::vector<Use> uses;
+    for (size_t i = 0; i < n; ++i) {
+        const ggml_tensor_xdna* t = nodes[i];
+        if (!t || t->op != GGML_OP_MUL_MAT || !t->src[0] || !t->src[1]) continue;
+        const ggml_tensor_xdna* b = t->src[1];
+        const bool xh = b->data && is_pinned_host(b->data), yh = t->data && is_pinned_host(t->data);
+        if (!xh && !yh) continue;
+        if (b->type != GGML_TYPE_F32 || b->ne[1] != 1 || b->ne[2] != 1 || b->ne[3] != 1 || t->ne[1] != 1 ||
+            t->ne[2] != 1 || t->ne[3] != 1)
+            return false;
+        if (xh) uses.push_back({b->data, static_cast<size_t>(b->ne[0]) * 4, false});
+        if (yh) uses.push_back({t->data, static_cast<size_t>(t->ne[0]) * 4, true});
+    }
+    if (uses.empty()) return false;
+    for (const Use& u : uses)
+        for (const Use& v : uses)
+            if ((u.out || v.out) && &u != &v && ranges_overlap(u.host, u.bytes, v.host, v.bytes) &&
+                !(u.host == v.host && !u.out && !v.out))
+                return false;
+    // one shadow per host range
+    std::vector<size_t> idx(uses.size());
+    for (size_t k = 0; k < uses.size(); ++k) {
+        size_t j = be->shadows.size();
+        for (size_t q = 0; q < be->shadows.size(); ++q)
+            if (be->shadows[q].host == uses[k].host && be->shadows[q].bytes >= uses[k].bytes) j = q;
+        if (j == be->shadows.size()) {
+            if (!may_alloc || be->shadows.size() >= kMaxShadows) return false;
+            void* d = nullptr;
+            if (cudaMalloc(&d, uses[k].bytes) != cudaSuccess) {
+                cudaGetLastError();
+                return false;
+            }
+            be->shadows.push_back({uses[k].host, uses[k].bytes, d});
+            ++be->scratch_gen;  // a graph holding other device copies is out of date
+        }
+        idx[k] = j;
+    }
+    sp->in.clear();
+    sp->out.clear();
+    for (size_t k = 0; k < uses.size(); ++k) {
+        std::vector<size_t>& v = uses[k].out ? sp->out : sp->in;
+        if (std::find(v.begin(), v.end(), idx[k]) == v.end()) v.push_back(idx[k]);
+    }
+    auto shadow_of = [&](const void* host) -> void* {
+        for (size_t k = 0; k < uses.size(); ++k)
+            if (uses[k].host == host) return be->shadows[idx[k]].dev;
+        return nullptr;
+    };
+    sp->nodes.clear();
+    sp->srcs.clear();
+    sp->nodes.reserve(n);
+    sp->srcs.reserve(n);
+    sp->ptrs.assign(nodes, nodes + n);
+    for (size_t i = 0; i < n; ++i) {
+        ggml_tensor_xdna* t = nodes[i];
+        if (!t || t->op != GGML_OP_MUL_MAT || !t->src[0] || !t->src[1]) continue;
+        void* xd = shadow_of(t->src[1]->data);
+        void* yd = shadow_of(t->data);
+        if (!xd && !yd) continue;
+        sp->nodes.push_back(*t);
+        ggml_tensor_xdna& c = sp->nodes.back();
+        if (xd) {
+            sp->srcs.push_back(*t->src[1]);
+            sp->srcs.back().data = xd;
+            c.src[1] = &sp->srcs.back();
+        }
+        if (yd) c.data = yd;
+        sp->ptrs[i] = &c;
+    }
+    return true;
+}
+
+
 }  // namespace
 }  // namespace xb
 
@@ -1259,6 +1372,7 @@ void ggml_backend_xdna_free(ggml_backend_t backend) {
         if (!be->xg.ok)
             for (void* p : be->xscratch)
                 if (p) cudaFree(p);
+        for (const Backend::HostShadow& h : be->shadows) cudaFree(h.dev);
         release_exchange(be);
         drop_graph(be);
         if (be->comm) nccl_api().CommDestroy(be->comm);
@@ -1387,11 +1501,28 @@ static bool run_nodes(Backend* be, ggml_tensor_xdna** nodes, size_t n_nodes) {
     return ok;
 }
 
+// The call on a shadowed list: host inputs in, the list, outputs out.
+static bool run_shadowed(Backend* be, const ShadowPlan& sp, size_t n) {
+    for (size_t j : sp.in) {
+        const Backend::HostShadow& h = be->shadows[j];
+        if (!cuda_ok(cudaMemcpyAsync(h.dev, h.host, h.bytes, cudaMemcpyHostToDevice, be->stream), "H2D inputs"))
+            return false;
+    }
+    if (!run_nodes(be, const_cast<ggml_tensor_xdna**>(sp.ptrs.data()), n)) return false;
+    for (size_t j : sp.out) {
+        const Backend::HostShadow& h = be->shadows[j];
+        if (!cuda_ok(cudaMemcpyAsync(h.host, h.dev, h.bytes, cudaMemcpyDeviceToHost, be->stream), "D2H outputs"))
+            return false;
+    }
+    return true;
+}
+
 // A node list that comes back unchanged (a decode step) is captured into a
 // CUDA graph on its second call and replayed from then on, when every operand
-// lives on this device and the backend drives one GPU (a sharded step's
-// exchange counts launches).  The first call runs eagerly, so the x scratch
-// the capture bakes in already has its final size.
+// lives on this device, or is a single F32 row in page-locked host memory
+// (run through a device copy, see shadow_host_operands).  The first call
+// runs eagerly, so the x scratch and device copies the capture bakes in
+// already have their final size.
 bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_xdna** nodes, size_t n_nodes) {
     if (!backend || !nodes || n_nodes == 0) return false;
     Backend* be = as_backend(backend);
@@ -1399,6 +1530,11 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
     std::lock_guard<std::mutex> lk(be->mtx);
     DeviceGuard g(be->dev);
     static const bool no_graph = getenv("XDNA_B200_NO_GRAPH") != nullptr || getenv("XDNA_TRACE_NODES") != nullptr;
+    // page-locked host operands: run a copy of the list on device copies of them
+    static thread_local ShadowPlan sp;
+    const bool shadowed = shadow_host_operands(be, nodes, n_nodes, true, &sp);
+    ggml_tensor_xdna** list = shadowed ? sp.ptrs.data() : nodes;
+    auto run_all = [&]() { return shadowed ? run_shadowed(be, sp, n_nodes) : run_nodes(be, nodes, n_nodes); };
     if (!no_graph) {
         std::vector<uint64_t> sig;
         graph_signature(nodes, n_nodes, &sig);
@@ -1407,7 +1543,7 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
             if (!be->graph_exec) {
                 cudaGraph_t graph = nullptr;
                 bool cap = cudaStreamBeginCapture(be->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
-                const bool ran = cap && run_nodes(be, nodes, n_nodes);
+                const bool ran = cap && run_all();
                 cap = cudaStreamEndCapture(be->stream, &graph) == cudaSuccess && cap;
                 if (ran && cap && graph && cudaGraphInstantiate(&be->graph_exec, graph, 0) == cudaSuccess) {
                     be->graph_gen = be->scratch_gen;
@@ -1425,10 +1561,10 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
         } else if (sig != be->graph_sig) {
             drop_graph(be);
             be->graph_sig.swap(sig);
-            be->graph_ok_sig = device_only_nodes(be, nodes, n_nodes);
+            be->graph_ok_sig = device_only_nodes(be, list, n_nodes);
         }
     }
-    const bool ok = run_nodes(be, nodes, n_nodes);
+    const bool ok = run_all();
     const bool flushed = flush(be);
     return ok && flushed;
 }
