@@ -338,6 +338,17 @@ struct Backend {
         void* dev;
     };
     std::vector<HostShadow> shadows;
+    // which MUL_MAT operands of the node list with signature pin_sig are
+    // page-locked host memory (bit 0: src1, bit 1: dst, per node index), so
+    // that a list seen again costs no pointer queries
+    struct PinnedOp {
+        size_t node;
+        unsigned mask;
+        const void* x;  // the node's src1 and dst data when classified
+        const void* y;
+    };
+    std::vector<uint64_t> pin_sig;
+    std::vector<PinnedOp> pin_ops;
     cudaGraphExec_t graph_exec = nullptr;
     uint64_t graph_gen = 0, scratch_gen = 0;
 };
@@ -1179,19 +1190,36 @@ struct ShadowPlan {
 };
 constexpr size_t kMaxShadows = 64;
 
-bool shadow_host_operands(Backend* be, ggml_tensor_xdna** nodes, size_t n, bool may_alloc, ShadowPlan* sp) {
+bool shadow_host_operands(Backend* be, ggml_tensor_xdna** nodes, size_t n, const std::vector<uint64_t>& sig,
+                          bool may_alloc, ShadowPlan* sp) {
     struct Use {
         void* host;
         size_t bytes;
         bool out;
     };
+    if (sig != be->pin_sig) {
+        be->pin_ops.clear();
+        for (size_t i = 0; i < n; ++i) {
+            const ggml_tensor_xdna* t = nodes[i];
+            if (!t || t->op != GGML_OP_MUL_MAT || !t->src[0] || !t->src[1]) continue;
+            const unsigned m = (t->src[1]->data && is_pinned_host(t->src[1]->data) ? 1u : 0u) |
+                               (t->data && is_pinned_host(t->data) ? 2u : 0u);
+            if (m) be->pin_ops.push_back({i, m, t->src[1]->data, t->data});
+        }
+        be->pin_sig = sig;
+    }
+    if (be->pin_ops.empty()) return false;
     std::vector<Use> uses;
-    for (size_t i = 0; i < n; ++i) {
-        const ggml_tensor_xdna* t = nodes[i];
-        if (!t || t->op != GGML_OP_MUL_MAT || !t->src[0] || !t->src[1]) continue;
+    for (const Backend::PinnedOp& op : be->pin_ops) {
+        // the same signature with the MUL_MATs at other node indices: classify again next call
+        const ggml_tensor_xdna* t = op.node < n ? nodes[op.node] : nullptr;
+        if (!t || t->op != GGML_OP_MUL_MAT || !t->src[0] || !t->src[1] || t->src[1]->data != op.x ||
+            t->data != op.y) {
+            be->pin_sig.clear();
+            return false;
+        }
         const ggml_tensor_xdna* b = t->src[1];
-        const bool xh = b->data && is_pinned_host(b->data), yh = t->data && is_pinned_host(t->data);
-        if (!xh && !yh) continue;
+        const bool xh = (op.mask & 1u) != 0, yh = (op.mask & 2u) != 0;
         if (b->type != GGML_TYPE_F32 || b->ne[1] != 1 || b->ne[2] != 1 || b->ne[3] != 1 || t->ne[1] != 1 ||
             t->ne[2] != 1 || t->ne[3] != 1)
             return false;
@@ -1531,13 +1559,13 @@ bool ggml_backend_xdna_compute_graph(ggml_backend_t backend, struct ggml_tensor_
     DeviceGuard g(be->dev);
     static const bool no_graph = getenv("XDNA_B200_NO_GRAPH") != nullptr || getenv("XDNA_TRACE_NODES") != nullptr;
     // page-locked host operands: run a copy of the list on device copies of them
+    std::vector<uint64_t> sig;
+    graph_signature(nodes, n_nodes, &sig);
     static thread_local ShadowPlan sp;
-    const bool shadowed = shadow_host_operands(be, nodes, n_nodes, true, &sp);
+    const bool shadowed = shadow_host_operands(be, nodes, n_nodes, sig, true, &sp);
     ggml_tensor_xdna** list = shadowed ? sp.ptrs.data() : nodes;
     auto run_all = [&]() { return shadowed ? run_shadowed(be, sp, n_nodes) : run_nodes(be, nodes, n_nodes); };
     if (!no_graph) {
-        std::vector<uint64_t> sig;
-        graph_signature(nodes, n_nodes, &sig);
         if (sig == be->graph_sig && be->graph_ok_sig) {
             if (be->graph_exec && be->graph_gen != be->scratch_gen) drop_graph(be);
             if (!be->graph_exec) {
